@@ -1,0 +1,184 @@
+/*
+ * lmoe_b200.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types.  Every entry point:
+ *   - launches asynchronously on `stream` (never on the legacy default stream unless the
+ *     caller passes it) and performs no host<->device synchronisation;
+ *   - never allocates device memory: outputs and workspaces are caller-owned;
+ *   - returns LMOE_OK (0), a negative LMOE_ERR_* for rejected arguments, or a positive
+ *     cudaError_t value when a CUDA call failed.
+ * Kernels that wait on their own pipelines bound every wait; a wait that gives up writes a
+ * nonzero word into the workspace's error slot (read it with lmoe_read_error).
+ *
+ * Each declaration names the light-moe interface it replaces (file:line in the reference
+ * repository Whitehall945/light-moe).
+ */
+#ifndef LMOE_B200_H_
+#define LMOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LMOE_OK 0
+#define LMOE_ERR_INVALID_ARG (-1)    /* shape / dtype / alignment / null pointer          */
+#define LMOE_ERR_UNSUPPORTED (-2)    /* valid request outside what the kernels implement  */
+#define LMOE_ERR_WORKSPACE (-3)      /* workspace missing or too small                    */
+#define LMOE_ERR_DEVICE (-4)         /* current device is not sm_100 / kernel error word  */
+
+typedef struct CUstream_st* lmoe_stream_t; /* identical to cudaStream_t */
+
+/* Library version as 10000*major + 100*minor + patch. */
+int lmoe_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* lmoe_status_string(int status);
+
+/* Copies the 32-bit device error word of a router / GEMM workspace to *out (synchronises
+ * `stream`).  0 means no kernel reported a problem. */
+int lmoe_read_error(const void* workspace, uint32_t* out, lmoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Router: gate logits + fp32 softmax + top-k + renormalise + histogram / offsets /       */
+/* stable permutation, in one kernel.                                                     */
+/* Replaces fused_gate_topk_cuda (csrc/fused_moe_ops.cu:145-200) and the count / offset / */
+/* argsort part of fused_gate_topk_permute_cuda (csrc/fused_moe_ops.cu:205-225).          */
+/* ------------------------------------------------------------------------------------ */
+
+/* Workspace bytes needed by lmoe_fused_gate_topk for these sizes. */
+size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts);
+
+/*
+ * hidden      bf16 [num_tokens, hidden]   row-major, 16-byte aligned, hidden % 64 == 0
+ * gate_weight bf16 [num_experts, hidden]  (nn.Linear layout, as the reference binding reads
+ *                                          E = gate_weight.size(0), fused_moe_ops.cu:155)
+ * gate_bias   fp32 [num_experts] or NULL (MoEGate(bias=True), moe_gate.py:159,171)
+ * 1 <= num_experts <= 256, 1 <= top_k <= min(16, num_experts)
+ * Outputs (any of the optional ones may be NULL):
+ *   ids          int32 [num_tokens, top_k]  descending probability, ties -> lower id
+ *   weights      fp32  [num_tokens, top_k]  renormalised to sum 1          (optional)
+ *   weights_bf16 bf16  [num_tokens, top_k]  same values rounded to bf16     (optional)
+ *   counts       int32 [num_experts]                                      (optional*)
+ *   offsets      int32 [num_experts + 1]  exclusive scan of counts        (optional*)
+ *   sorted_idx   int32 [num_tokens*top_k]  flat index t*top_k+j ordered by
+ *                (expert, token, slot)                                    (optional*)
+ *   logits       fp32  [num_tokens, num_experts]  gate logits (+bias), for checking
+ * (*) counts, offsets and sorted_idx are produced together: pass all three or none.
+ */
+int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
+                         int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                         int32_t* ids, float* weights, void* weights_bf16,
+                         int32_t* counts, int32_t* offsets, int32_t* sorted_idx, float* logits,
+                         void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Row gather / weighted combine                                                          */
+/* ------------------------------------------------------------------------------------ */
+
+/* permuted[r, :] = hidden[sorted_idx[r] / top_k, :] for r < rows (bf16, hidden % 8 == 0).
+ * Replaces the expand + index_select of fused_gate_topk_permute_cuda
+ * (csrc/fused_moe_ops.cu:227-228) and permute_tokens (python/light_moe/ops/grouped_gemm.py:
+ * 202-247). */
+int lmoe_permute_rows(const void* hidden, const int32_t* sorted_idx, int64_t rows, int hidden_size,
+                      int top_k, void* permuted, lmoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* int4 weight format (defined by this library; the reference only has the unused flag    */
+/* EngineConfig.use_int4_quantization, python/light_moe/engine/executor.py:44-48).        */
+/*   qweight uint8 [rows, K/2]: byte b holds k=2b (low nibble) and k=2b+1 (high nibble),   */
+/*           each stored as q+8;  scales fp16 [rows, K/group]: s = fp16(max|w|/7);          */
+/*   q = clamp(rint(w / s), -8, 7);  dequantised value = bf16_rn(q * s).                   */
+/* ------------------------------------------------------------------------------------ */
+
+/* w: [rows, K] bf16 (w_is_fp32 == 0) or fp32 (w_is_fp32 != 0). */
+int lmoe_quantize_w4(const void* w, int w_is_fp32, int64_t rows, int K, int group_size,
+                     uint8_t* qweight, uint16_t* scales, lmoe_stream_t stream);
+
+/* out: bf16 [rows, K]. */
+int lmoe_dequantize_w4(const uint8_t* qweight, const uint16_t* scales, int64_t rows, int K,
+                       int group_size, void* out, lmoe_stream_t stream);
+
+/* Sizes of the device ("prepacked") layout streamed by the W4A16 GEMM for `num_experts`
+ * matrices of [rows, K]; paired != 0 interleaves two such matrices (gate w1 and up w3) by
+ * 64-row blocks, giving 2*rows rows.  K % 64 == 0, group_size % 64 == 0, rows % 128 == 0
+ * (rows % 64 == 0 when paired). */
+int lmoe_w4_prepacked_sizes(int num_experts, int rows, int K, int group_size, int paired,
+                            size_t* packed_bytes, size_t* scale_bytes);
+
+/* Canonical int4 weights [num_experts, rows, K/2] (+ scales) -> prepacked layout.  Pass the
+ * up-projection as qweight_b / scales_b to build the paired gate/up layout, else NULL. */
+int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_a,
+                    const uint8_t* qweight_b, const uint16_t* scales_b,
+                    int num_experts, int rows, int K, int group_size,
+                    uint8_t* packed, uint16_t* packed_scales, lmoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Grouped GEMMs.  Rows [offsets[e], offsets[e+1]) of `input` (bf16 [total_rows, K]) are  */
+/* multiplied by expert e's weight matrix ([N, K]); offsets are int32 or int64 [E+1] and  */
+/* are read on the device (no host copy).  Workspace: lmoe_gemm_workspace_bytes().        */
+/* ------------------------------------------------------------------------------------ */
+
+size_t lmoe_gemm_workspace_bytes(void);
+
+/* Dense bf16 weights [num_experts, N, K].  output bf16 [total_rows, N]; with zero_fill the
+ * rows outside every expert range are zeroed first.
+ * Replaces grouped_gemm_cuda (csrc/grouped_gemm.cu:11-43), which zero-fills (:24), copies
+ * the offsets to the host (:27) and runs one cuBLAS GEMM per expert (:30-40). */
+int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const void* weights, int N,
+                           const void* expert_offsets, int offsets_are_int64, int num_experts,
+                           int zero_fill, void* output, void* workspace, size_t workspace_bytes,
+                           lmoe_stream_t stream);
+
+/* W4A16: prepacked int4 weights (N rows per expert, N % 128 == 0), fp32 accumulation.
+ * epilogue 0: output[r, n] = acc                               (ldo >= N)
+ * epilogue 1: SwiGLU over a paired gate/up matrix of N = 2*F rows:
+ *             output[r, f] = silu(gate[r, f]) * up[r, f]         (ldo >= F)
+ * epilogue 2: output[dest_rows[r], n] = row_scale[r] * acc       (NULL = identity / 1)
+ * max_rows_per_expert: an upper bound of any expert's row count if known (0 = unknown);
+ * small bounds select the decode-sized tiles.
+ * New op; the reference has no W4A16 GEMM (SparseMoEBlockFast's GroupedLinear calls,
+ * python/light_moe/model/moe_block.py:249-256, are its dense counterpart). */
+int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
+                            const uint16_t* packed_scales, int N, int group_size,
+                            const void* expert_offsets, int offsets_are_int64, int num_experts,
+                            int epilogue, const int32_t* dest_rows, const float* row_scale,
+                            int64_t max_rows_per_expert, void* output, int64_t ldo,
+                            void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* The W4A16 MoE layer: router -> gather -> gate/up GEMM (SwiGLU) -> down GEMM (routing   */
+/* weight, scatter to slot) -> per-token combine, all on `stream` without host syncs.     */
+/* Replaces SparseMoEBlock.forward / SparseMoEBlockFast.forward                           */
+/* (python/light_moe/model/moe_block.py:119-169, :216-274) with int4 experts.             */
+/* ------------------------------------------------------------------------------------ */
+
+size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int ffn_size,
+                                      int num_experts, int top_k, int num_shared);
+
+/*
+ * x        bf16 [num_tokens, hidden_size]    (hidden_size % 128 == 0)
+ * gate_*   router weight bf16 [num_experts, hidden_size], optional fp32 bias
+ * w13      paired prepacked gate/up weights of num_experts + num_shared experts
+ *          (routed experts first), each 2*ffn_size x hidden_size
+ * w2       prepacked down weights, each hidden_size x ffn_size
+ * num_shared always-on experts (weight 1, every token), 0 for Mixtral
+ * y        bf16 [num_tokens, hidden_size]
+ * ids_out / weights_out: optional copies of the routing (int32 / fp32 [num_tokens, top_k])
+ */
+int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidden_size,
+                         const void* gate_weight, const float* gate_bias, int num_experts,
+                         int top_k, int num_shared,
+                         const uint8_t* w13_packed, const uint16_t* w13_scales,
+                         const uint8_t* w2_packed, const uint16_t* w2_scales,
+                         int ffn_size, int group_size, void* y,
+                         int32_t* ids_out, float* weights_out,
+                         void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LMOE_B200_H_ */

@@ -1,0 +1,46 @@
+// grouped_gemm.h -- internal interface of the persistent grouped GEMM (grouped_gemm.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace lmoe {
+
+constexpr int kMaxGemmExperts = 256;
+
+enum GemmMode : int {
+  kModePlain = 0,    // out[r, n] = acc
+  kModeSwiGLU = 1,   // tile rows j / j+64 = gate / up of feature fb*64+j: out[r, f] = silu(g) * u
+  kModeScatter = 2,  // out[dest[r], n] = row_scale[r] * acc
+};
+
+struct GemmProblem {
+  // activations: bf16 [total_rows, K], row pitch ldx elements
+  const void* x = nullptr;
+  int64_t ldx = 0;
+  int64_t total_rows = 0;
+  int K = 0;
+  // expert row ranges [num_experts + 1] (int32, or int64 when offsets_i64)
+  const void* offsets = nullptr;
+  int offsets_i64 = 0;
+  int num_experts = 0;
+  // weights: either W4 prepacked (wq + wscale) or bf16 [num_experts, N, K] (w)
+  const uint8_t* wq = nullptr;
+  const uint16_t* wscale = nullptr;
+  int group_size = 0;
+  const void* w = nullptr;
+  int N = 0;  // weight rows per expert (for SwiGLU: 2 * features)
+  // epilogue
+  int mode = kModePlain;
+  void* out = nullptr;
+  int64_t ldo = 0;
+  const int32_t* dest = nullptr;
+  const float* row_scale = nullptr;
+  uint32_t* err = nullptr;
+  // a known upper bound of rows per expert (0 = unknown); small values pick the decode tiles
+  int64_t max_rows_per_expert_hint = 0;
+};
+
+int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream);
+
+}  // namespace lmoe

@@ -1,0 +1,93 @@
+// host_util.cu -- device-info cache, TMA descriptor encoding and the small C-ABI utilities.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "host_util.h"
+
+namespace lmoe {
+
+namespace {
+constexpr int kMaxDevices = 64;
+DeviceInfo g_info[kMaxDevices];
+std::mutex g_info_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+}  // namespace
+
+int get_device_info(DeviceInfo* out) {
+  int dev = 0;
+  LMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return LMOE_ERR_DEVICE;
+  {
+    std::lock_guard<std::mutex> lk(g_info_mu);
+    if (g_info[dev].device == dev) {
+      *out = g_info[dev];
+      return LMOE_OK;
+    }
+  }
+  DeviceInfo d;
+  d.device = dev;
+  LMOE_CUDA_TRY(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev));
+  LMOE_CUDA_TRY(cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+  LMOE_CUDA_TRY(cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+  int smem = 0;
+  LMOE_CUDA_TRY(cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  d.max_smem_optin = (size_t)smem;
+  std::lock_guard<std::mutex> lk(g_info_mu);
+  g_info[dev] = d;
+  *out = d;
+  return LMOE_OK;
+}
+
+int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                   uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols,
+                   bool swizzle128) {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (!g_encode) return LMOE_ERR_DEVICE;
+  if (!aligned16(base) || (row_stride_bytes % 16) != 0) return LMOE_ERR_INVALID_ARG;
+  if (box_rows == 0 || box_rows > 256 || box_cols == 0 || box_cols > 256) return LMOE_ERR_INVALID_ARG;
+  if (swizzle128 && box_cols * elem_bytes != 128) return LMOE_ERR_INVALID_ARG;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_INVALID_ARG;
+}
+
+}  // namespace lmoe
+
+extern "C" int lmoe_version(void) { return 100; }
+
+extern "C" const char* lmoe_status_string(int status) {
+  switch (status) {
+    case LMOE_OK: return "ok";
+    case LMOE_ERR_INVALID_ARG: return "invalid argument (shape, dtype, alignment or null pointer)";
+    case LMOE_ERR_UNSUPPORTED: return "unsupported configuration";
+    case LMOE_ERR_WORKSPACE: return "workspace missing or too small";
+    case LMOE_ERR_DEVICE: return "device is not sm_100 or a kernel reported an error";
+    default: break;
+  }
+  if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
+  return "unknown status";
+}
+
+extern "C" int lmoe_read_error(const void* workspace, uint32_t* out, lmoe_stream_t stream) {
+  if (!workspace || !out) return LMOE_ERR_INVALID_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  LMOE_CUDA_TRY(cudaMemcpyAsync(out, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  LMOE_CUDA_TRY(cudaStreamSynchronize(s));
+  return LMOE_OK;
+}

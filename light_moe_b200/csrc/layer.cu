@@ -1,0 +1,377 @@
+// layer.cu -- C-ABI entry points for the grouped GEMMs and the W4A16 MoE layer, plus the
+// small glue kernels between them (routing-table expansion, row gather, int4 prepacking,
+// weighted combine).
+//
+// Layer data flow (all on one stream, no host synchronisation):
+//   router     x, Wg          -> ids, weights, counts, offsets, sorted_idx      (router.cu)
+//   table      sorted_idx     -> per dispatched row: source token, output slot, weight;
+//                                expert offsets extended with the always-on shared experts
+//   gather     x              -> xp [R, d]   rows in expert order (permute)
+//   gate/up    xp, W13 (int4) -> h  [R, ffn] = silu(x W1^T) * (x W3^T)   (SwiGLU epilogue)
+//   down       h,  W2  (int4) -> o  [T*(k+S), d] = weight * (h W2^T), scattered to its slot
+//   combine    o              -> y  [T, d]   = sum over the token's slots (fixed order)
+// Reference: SparseMoEBlock.forward (python/light_moe/model/moe_block.py:119-169) and
+// SparseMoEBlockFast.forward (moe_block.py:216-274).
+#include <cuda_bf16.h>
+
+#include "grouped_gemm.h"
+#include "host_util.h"
+#include "ptx.cuh"
+#include "w4_layout.cuh"
+
+namespace lmoe {
+namespace {
+
+// ------------------------------------------------------------------------------------ prepack
+// One thread per output 16-byte chunk: (e, fb, kb, half, row).
+__global__ void prepack_w4_kernel(const uint8_t* __restrict__ qa, const uint8_t* __restrict__ qb, int E, int rows_in,
+                                  int K, uint8_t* __restrict__ out, int paired) {
+  const int NB = paired ? rows_in / 64 : rows_in / kW4BlockRows;
+  const int KB = K / kW4BlockK;
+  const int64_t total = (int64_t)E * NB * KB * 2 * kW4BlockRows;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int r = (int)(i % kW4BlockRows);
+  int64_t rest = i / kW4BlockRows;
+  const int h = (int)(rest % 2);
+  rest /= 2;
+  const int kb = (int)(rest % KB);
+  rest /= KB;
+  const int fb = (int)(rest % NB);
+  const int e = (int)(rest / NB);
+  const uint8_t* src;
+  int64_t srow;
+  if (paired) {
+    src = r < 64 ? qa : qb;
+    srow = (int64_t)e * rows_in + fb * 64 + (r & 63);
+  } else {
+    src = qa;
+    srow = (int64_t)e * rows_in + fb * kW4BlockRows + r;
+  }
+  const uint4 c = *reinterpret_cast<const uint4*>(src + srow * (K / 2) + (kb * kW4BlockK + h * 32) / 2);
+  uint4 o;
+  o.x = w4_interleave_word(c.x);
+  o.y = w4_interleave_word(c.y);
+  o.z = w4_interleave_word(c.z);
+  o.w = w4_interleave_word(c.w);
+  reinterpret_cast<uint4*>(out)[i] = o;
+}
+
+__global__ void prepack_scales_kernel(const uint16_t* __restrict__ sa, const uint16_t* __restrict__ sb, int E,
+                                      int rows_in, int G, uint16_t* __restrict__ out, int paired) {
+  const int NB = paired ? rows_in / 64 : rows_in / kW4BlockRows;
+  const int64_t total = (int64_t)E * NB * G * kW4BlockRows;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int r = (int)(i % kW4BlockRows);
+  int64_t rest = i / kW4BlockRows;
+  const int g = (int)(rest % G);
+  rest /= G;
+  const int fb = (int)(rest % NB);
+  const int e = (int)(rest / NB);
+  if (paired) {
+    const uint16_t* src = r < 64 ? sa : sb;
+    out[i] = src[((int64_t)e * rows_in + fb * 64 + (r & 63)) * G + g];
+  } else {
+    out[i] = sa[((int64_t)e * rows_in + fb * kW4BlockRows + r) * G + g];
+  }
+}
+
+// ------------------------------------------------------------------------------------ routing table
+// rows r < T*k come from the router's sorted order; rows T*k + s*T + t are token t for
+// shared expert s.  Slots are [T, k + S]: routed slot j, then shared slot k + s.
+__global__ void routing_table_kernel(const int32_t* __restrict__ sorted_idx, const float* __restrict__ weights,
+                                     const int32_t* __restrict__ offsets, int T, int k, int E, int S,
+                                     int32_t* __restrict__ src_tok, int32_t* __restrict__ dest,
+                                     float* __restrict__ scale, int32_t* __restrict__ offsets_ext) {
+  const int64_t Rr = (int64_t)T * k;
+  const int64_t R = Rr + (int64_t)S * T;
+  const int slots = k + S;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < R) {
+    if (i < Rr) {
+      const int f = sorted_idx[i];
+      const int t = f / k;
+      const int j = f - t * k;
+      src_tok[i] = t;
+      dest[i] = t * slots + j;
+      scale[i] = weights[f];
+    } else {
+      const int64_t u = i - Rr;
+      const int s = (int)(u / T);
+      const int t = (int)(u - (int64_t)s * T);
+      src_tok[i] = t;
+      dest[i] = t * slots + k + s;
+      scale[i] = 1.0f;
+    }
+  }
+  if (i <= E + S) {
+    offsets_ext[i] = (i <= E) ? offsets[i] : (int32_t)(Rr + (int64_t)(i - E) * T);
+  }
+}
+
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ src_tok, int64_t rows,
+                                   int vec_per_row, uint4* __restrict__ out) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint4* s = x + (int64_t)src_tok[r] * vec_per_row;
+    uint4* d = out + r * vec_per_row;
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) d[i] = __ldg(s + i);
+  }
+}
+
+// y[t, :] = sum_{j < slots} o[t*slots + j, :]  (fp32 accumulation in slot order, bf16 out)
+__global__ void combine_slots_kernel(const __nv_bfloat162* __restrict__ o, int64_t T, int slots, int d2,
+                                     __nv_bfloat162* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * d2) return;
+  const int64_t t = i / d2;
+  const int c = (int)(i - t * d2);
+  float ax = 0.0f, ay = 0.0f;
+  const __nv_bfloat162* p = o + t * slots * d2 + c;
+  for (int j = 0; j < slots; ++j) {
+    const float2 v = __bfloat1622float2(p[(int64_t)j * d2]);
+    ax = __fadd_rn(ax, v.x);
+    ay = __fadd_rn(ay, v.y);
+  }
+  y[i] = __floats2bfloat162_rn(ax, ay);
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace carve-up of the layer (all 256-byte aligned).
+struct LayerWs {
+  size_t router, ids, wts, counts, offs, sidx, src, dest, scale, offx, xp, h, o, total;
+};
+
+LayerWs layer_ws(int64_t T, int d, int ffn, int E, int k, int S) {
+  LayerWs w{};
+  const int64_t R = T * k + (int64_t)S * T;
+  size_t p = 0;
+  // the router workspace comes first: its leading error word is shared by every kernel of
+  // the layer, so reading word 0 of the layer workspace reports any of them
+  w.router = p;
+  p = align256(p + lmoe_router_workspace_bytes(T, E));
+  w.ids = p; p = align256(p + sizeof(int32_t) * T * k);
+  w.wts = p; p = align256(p + sizeof(float) * T * k);
+  w.counts = p; p = align256(p + sizeof(int32_t) * E);
+  w.offs = p; p = align256(p + sizeof(int32_t) * (E + 1));
+  w.sidx = p; p = align256(p + sizeof(int32_t) * T * k);
+  w.src = p; p = align256(p + sizeof(int32_t) * R);
+  w.dest = p; p = align256(p + sizeof(int32_t) * R);
+  w.scale = p; p = align256(p + sizeof(float) * R);
+  w.offx = p; p = align256(p + sizeof(int32_t) * (E + S + 1));
+  w.xp = p; p = align256(p + sizeof(uint16_t) * R * d);
+  w.h = p; p = align256(p + sizeof(uint16_t) * R * ffn);
+  w.o = p; p = align256(p + sizeof(uint16_t) * T * (k + S) * d);
+  w.total = p;
+  return w;
+}
+
+}  // namespace
+}  // namespace lmoe
+
+using namespace lmoe;
+
+// ---------------------------------------------------------------------------------- C ABI
+
+extern "C" int lmoe_w4_prepacked_sizes(int num_experts, int rows, int K, int group_size, int paired,
+                                       size_t* packed_bytes, size_t* scale_bytes) {
+  LMOE_ARG_CHECK(num_experts >= 1 && rows > 0 && K > 0 && group_size > 0);
+  LMOE_ARG_CHECK(K % kW4BlockK == 0 && K % group_size == 0 && group_size % kW4BlockK == 0);
+  LMOE_ARG_CHECK(paired ? rows % 64 == 0 : rows % kW4BlockRows == 0);
+  const int64_t out_rows = (int64_t)(paired ? 2 * rows : rows);
+  if (packed_bytes) *packed_bytes = (size_t)num_experts * out_rows * (K / 2);
+  if (scale_bytes) *scale_bytes = (size_t)num_experts * out_rows * (K / group_size) * sizeof(uint16_t);
+  return LMOE_OK;
+}
+
+extern "C" int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_a, const uint8_t* qweight_b,
+                               const uint16_t* scales_b, int num_experts, int rows, int K, int group_size,
+                               uint8_t* packed, uint16_t* packed_scales, lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int paired = qweight_b != nullptr;
+  size_t pb = 0, sb = 0;
+  int st = lmoe_w4_prepacked_sizes(num_experts, rows, K, group_size, paired, &pb, &sb);
+  if (st != LMOE_OK) return st;
+  LMOE_ARG_CHECK(qweight_a && scales_a && packed && packed_scales);
+  LMOE_ARG_CHECK(!paired || scales_b);
+  LMOE_ARG_CHECK(aligned16(qweight_a) && (!paired || aligned16(qweight_b)) && aligned16(packed));
+  const int threads = 256;
+  const int64_t chunks = (int64_t)pb / 16;
+  prepack_w4_kernel<<<(unsigned)((chunks + threads - 1) / threads), threads, 0, stream>>>(
+      qweight_a, qweight_b, num_experts, rows, K, packed, paired);
+  LMOE_CUDA_TRY(cudaGetLastError());
+  const int64_t ns = (int64_t)sb / 2;
+  prepack_scales_kernel<<<(unsigned)((ns + threads - 1) / threads), threads, 0, stream>>>(
+      scales_a, scales_b, num_experts, rows, K / group_size, packed_scales, paired);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" size_t lmoe_gemm_workspace_bytes(void) { return 256; }
+
+extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const void* weights, int N,
+                                      const void* expert_offsets, int offsets_are_int64, int num_experts,
+                                      int zero_fill, void* output, void* workspace, size_t workspace_bytes,
+                                      lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1);
+  LMOE_ARG_CHECK(input && weights && expert_offsets && output);
+  LMOE_ARG_CHECK(aligned16(input) && aligned16(weights) && K % 64 == 0);
+  if (!workspace || workspace_bytes < 256) return LMOE_ERR_WORKSPACE;
+  if (zero_fill && total_rows > 0)
+    LMOE_CUDA_TRY(cudaMemsetAsync(output, 0, (size_t)total_rows * N * sizeof(uint16_t), stream));
+  LMOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, 256, stream));
+  GemmProblem p;
+  p.x = input;
+  p.ldx = K;
+  p.total_rows = total_rows;
+  p.K = K;
+  p.offsets = expert_offsets;
+  p.offsets_i64 = offsets_are_int64;
+  p.num_experts = num_experts;
+  p.w = weights;
+  p.N = N;
+  p.mode = kModePlain;
+  p.out = output;
+  p.ldo = N;
+  p.err = static_cast<uint32_t*>(workspace);
+  return run_grouped_gemm(p, stream);
+}
+
+extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
+                                       const uint16_t* packed_scales, int N, int group_size,
+                                       const void* expert_offsets, int offsets_are_int64, int num_experts,
+                                       int epilogue, const int32_t* dest_rows, const float* row_scale,
+                                       int64_t max_rows_per_expert, void* output, int64_t ldo, void* workspace,
+                                       size_t workspace_bytes, lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1);
+  LMOE_ARG_CHECK(input && packed && packed_scales && expert_offsets && output);
+  LMOE_ARG_CHECK(aligned16(input) && aligned16(packed) && aligned16(packed_scales));
+  LMOE_ARG_CHECK(epilogue >= kModePlain && epilogue <= kModeScatter);
+  LMOE_ARG_CHECK(ldo >= (epilogue == kModeSwiGLU ? N / 2 : N));
+  if (!workspace || workspace_bytes < 256) return LMOE_ERR_WORKSPACE;
+  LMOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, 256, stream));
+  GemmProblem p;
+  p.x = input;
+  p.ldx = K;
+  p.total_rows = total_rows;
+  p.K = K;
+  p.offsets = expert_offsets;
+  p.offsets_i64 = offsets_are_int64;
+  p.num_experts = num_experts;
+  p.wq = packed;
+  p.wscale = packed_scales;
+  p.group_size = group_size;
+  p.N = N;
+  p.mode = epilogue;
+  p.out = output;
+  p.ldo = ldo;
+  p.dest = dest_rows;
+  p.row_scale = row_scale;
+  p.err = static_cast<uint32_t*>(workspace);
+  p.max_rows_per_expert_hint = max_rows_per_expert;
+  return run_grouped_gemm(p, stream);
+}
+
+extern "C" size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int ffn_size, int num_experts,
+                                                 int top_k, int num_shared) {
+  if (num_tokens < 0 || hidden_size <= 0 || ffn_size <= 0 || num_experts <= 0 || top_k <= 0 || num_shared < 0)
+    return 0;
+  return layer_ws(num_tokens, hidden_size, ffn_size, num_experts, top_k, num_shared).total;
+}
+
+extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidden_size, const void* gate_weight,
+                                    const float* gate_bias, int num_experts, int top_k, int num_shared,
+                                    const uint8_t* w13_packed, const uint16_t* w13_scales, const uint8_t* w2_packed,
+                                    const uint16_t* w2_scales, int ffn_size, int group_size, void* y,
+                                    int32_t* ids_out, float* weights_out, void* workspace, size_t workspace_bytes,
+                                    lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int64_t T = num_tokens;
+  const int d = hidden_size, E = num_experts, k = top_k, S = num_shared, F = ffn_size;
+  LMOE_ARG_CHECK(T >= 0 && d > 0 && F > 0 && E >= 1 && k >= 1 && S >= 0);
+  LMOE_ARG_CHECK(E + S <= kMaxGemmExperts);
+  LMOE_ARG_CHECK(d % 128 == 0 && F % 64 == 0 && group_size % 64 == 0 && d % group_size == 0 && F % group_size == 0);
+  LMOE_ARG_CHECK(x && gate_weight && w13_packed && w13_scales && w2_packed && w2_scales && y);
+  const LayerWs L = layer_ws(T, d, F, E, k, S);
+  if (!workspace || workspace_bytes < L.total || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
+  if (T == 0) return LMOE_OK;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto at = [&](size_t off) { return static_cast<void*>(ws + off); };
+  int32_t* ids = ids_out ? ids_out : static_cast<int32_t*>(at(L.ids));
+  float* wts = weights_out ? weights_out : static_cast<float*>(at(L.wts));
+  int32_t* counts = static_cast<int32_t*>(at(L.counts));
+  int32_t* offs = static_cast<int32_t*>(at(L.offs));
+  int32_t* sidx = static_cast<int32_t*>(at(L.sidx));
+  int32_t* src = static_cast<int32_t*>(at(L.src));
+  int32_t* dest = static_cast<int32_t*>(at(L.dest));
+  float* scale = static_cast<float*>(at(L.scale));
+  int32_t* offx = static_cast<int32_t*>(at(L.offx));
+  uint32_t* err = static_cast<uint32_t*>(at(L.router));  // zeroed by the router call
+  const int64_t R = T * k + (int64_t)S * T;
+
+  int st = lmoe_fused_gate_topk(x, gate_weight, gate_bias, T, d, E, k, ids, wts, nullptr, counts, offs, sidx,
+                                nullptr, at(L.router), lmoe_router_workspace_bytes(T, E), stream_);
+  if (st != LMOE_OK) return st;
+  {
+    const int threads = 256;
+    const int64_t n = R > (E + S + 1) ? R : (E + S + 1);
+    routing_table_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+        sidx, wts, offs, (int)T, k, E, S, src, dest, scale, offx);
+    LMOE_CUDA_TRY(cudaGetLastError());
+    const int vec = d / 8;
+    const int64_t grid = R < 65535 * 4 ? R : 65535 * 4;
+    gather_rows_kernel<<<(unsigned)grid, vec >= 256 ? 256 : vec, 0, stream>>>(
+        static_cast<const uint4*>(x), src, R, vec, static_cast<uint4*>(at(L.xp)));
+    LMOE_CUDA_TRY(cudaGetLastError());
+  }
+  // a routed expert receives at most T rows; shared experts exactly T
+  const int64_t hint = T;
+  GemmProblem g1;
+  g1.x = at(L.xp);
+  g1.ldx = d;
+  g1.total_rows = R;
+  g1.K = d;
+  g1.offsets = offx;
+  g1.num_experts = E + S;
+  g1.wq = w13_packed;
+  g1.wscale = w13_scales;
+  g1.group_size = group_size;
+  g1.N = 2 * F;
+  g1.mode = kModeSwiGLU;
+  g1.out = at(L.h);
+  g1.ldo = F;
+  g1.err = err;
+  g1.max_rows_per_expert_hint = hint;
+  st = run_grouped_gemm(g1, stream);
+  if (st != LMOE_OK) return st;
+  GemmProblem g2;
+  g2.x = at(L.h);
+  g2.ldx = F;
+  g2.total_rows = R;
+  g2.K = F;
+  g2.offsets = offx;
+  g2.num_experts = E + S;
+  g2.wq = w2_packed;
+  g2.wscale = w2_scales;
+  g2.group_size = group_size;
+  g2.N = d;
+  g2.mode = kModeScatter;
+  g2.out = at(L.o);
+  g2.ldo = d;
+  g2.dest = dest;
+  g2.row_scale = scale;
+  g2.err = err;
+  g2.max_rows_per_expert_hint = hint;
+  st = run_grouped_gemm(g2, stream);
+  if (st != LMOE_OK) return st;
+  {
+    const int threads = 256;
+    const int64_t n = T * (d / 2);
+    combine_slots_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+        static_cast<const __nv_bfloat162*>(at(L.o)), T, k + S, d / 2, static_cast<__nv_bfloat162*>(y));
+    LMOE_CUDA_TRY(cudaGetLastError());
+  }
+  return LMOE_OK;
+}

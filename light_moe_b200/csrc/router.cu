@@ -1,0 +1,469 @@
+// router.cu -- the fused MoE router for B200 (sm_100a).
+//
+// One kernel computes, for every token:
+//   logits = x . W^T (+ b)          tcgen05 MMA, bf16 x bf16 -> fp32 in tensor memory
+//   p      = softmax(logits)        fp32, exp of (logit - max), sequential sum, reciprocal
+//   top-k  by p                     ties keep the lower expert id
+//   w      = p_topk / sum(p_topk)   reciprocal-multiply renormalisation
+// and, over all tokens, the per-expert histogram, its exclusive scan (offsets) and the
+// stable permutation sorted_idx (expert, token, slot) of the flattened assignment list.
+//
+// Reference semantics: csrc/fused_moe_ops.cu:145-231 (fused_gate_topk_cuda,
+// fused_softmax_topk_kernel, fused_gate_topk_permute_cuda) and
+// python/light_moe/ops/moe_gate.py:39-77, :202-214.  The reference runs a cuBLAS fp32 GEMM
+// after two dtype-conversion copies, a CUDA-core softmax/top-k kernel for E in {8,16} and
+// top-2 only, and ~2E+6 ATen launches for counts/offsets/argsort; here it is one kernel.
+//
+// Structure (persistent, one CTA per SM, 128 tokens per tile, 6 warps):
+//   warp 0     TMA producer: x tile [128 x 64] and W tile [Epad x 64] per stage (128B swizzle)
+//   warp 1     MMA issuer: 4 x tcgen05.mma (M=128, N=Epad, K=16) per stage into one of two
+//              TMEM accumulators
+//   warps 2-5  epilogue: one token row per thread (TMEM lane), softmax / top-k / renormalise,
+//              per-tile expert bitmap for the permutation
+// When the permutation is requested the kernel is launched cooperatively and, after a grid
+// barrier, every CTA scans the per-tile counts and scatters its tokens into sorted_idx.
+#include <cuda_bf16.h>
+
+#include "host_util.h"
+#include "lmoe_math.cuh"
+#include "ptx.cuh"
+
+namespace lmoe {
+namespace {
+
+constexpr int kBM = 128;          // tokens per tile
+constexpr int kBK = 64;           // hidden elements per stage (one 128-byte swizzle row)
+constexpr int kThreads = 192;     // 6 warps
+constexpr int kMaxStages = 8;
+constexpr int kMaxExperts = 256;
+constexpr uint32_t kSite = 0x100u;
+
+struct RouterArgs {
+  const float* bias;
+  int32_t* ids;
+  float* weights;
+  __nv_bfloat16* weights_bf16;
+  float* logits;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* sorted_idx;
+  int32_t* tile_counts;   // [num_tiles, E]
+  uint32_t* tile_bits;    // [num_tiles, E, 4] : bit r of word r/32 set if token row r picked e
+  uint32_t* grid_sync;    // arrival counter for the grid barrier (zeroed by the host)
+  uint32_t* err;          // device error word (zeroed by the host)
+  int T, d, E, Epad, k, num_tiles, stages;
+  uint32_t stage_bytes;   // x tile + W tile, multiple of 1024
+  uint32_t tmem_cols;
+  int do_perm;
+};
+
+struct __align__(8) RouterHdr {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  float bias[kMaxExperts];
+  uint32_t bits[kMaxExperts * 4];
+  int32_t total[kMaxExperts];
+  int32_t offs[kMaxExperts + 1];
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int KMAX>
+__global__ void __launch_bounds__(kThreads, 1)
+    router_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                  const RouterArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  RouterHdr* h = reinterpret_cast<RouterHdr*>(base + a.stages * a.stage_bytes);
+  volatile int* abort_flag = &h->abort;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nk = a.d / kBK;
+
+  if (tid == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&h->full[s], 1);
+      mbar_init(&h->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&h->acc_full[b], 1);
+      mbar_init(&h->acc_empty[b], 128);
+    }
+    mbar_init(&h->mma_done, 1);
+    h->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(&h->tmem_base, a.tmem_cols);
+    tmem_relinquish();
+  }
+  for (int e = tid; e < a.E; e += kThreads) h->bias[e] = a.bias ? a.bias[e] : 0.0f;
+  for (int i = tid; i < a.E * 4; i += kThreads) h->bits[i] = 0u;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = h->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const int s = it % a.stages;
+          const uint32_t ph = (it / a.stages) & 1u;
+          if (!mbar_wait(&h->empty[s], ph ^ 1u, a.err, abort_flag, kSite + 1)) { ok = false; break; }
+          uint8_t* xs = base + s * a.stage_bytes;
+          uint8_t* ws = xs + kBM * kBK * 2;
+          mbar_arrive_expect_tx(&h->full[s], a.stage_bytes);
+          tma_load_2d(xs, &tm_x, &h->full[s], kc * kBK, tile * kBM);
+          tma_load_2d(ws, &tm_w, &h->full[s], kc * kBK, 0);
+        }
+      }
+      // never leave the CTA with bulk copies still landing in shared memory
+      const uint32_t issued = it;
+      const uint32_t first = issued > (uint32_t)a.stages ? issued - a.stages : 0u;
+      for (uint32_t j = first; j < issued; ++j) {
+        const int s = j % a.stages;
+        mbar_wait(&h->full[s], (j / a.stages) & 1u, a.err, nullptr, kSite + 2);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, a.Epad);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++lt) {
+        const uint32_t acc = lt & 1u;
+        if (!mbar_wait(&h->acc_empty[acc], ((lt >> 1) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * a.Epad;
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const int s = it % a.stages;
+          if (!mbar_wait(&h->full[s], (it / a.stages) & 1u, a.err, abort_flag, kSite + 4)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t xa = smem_u32(base + s * a.stage_bytes);
+          const uint32_t wa = xa + kBM * kBK * 2;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            mma_ss(d_tmem, sdesc_k_sw128(xa + kk * 32), sdesc_k_sw128(wa + kk * 32), idesc,
+                   (kc | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&h->empty[s]);
+        }
+        if (ok) mma_commit(&h->acc_full[acc]);
+      }
+      // all issued MMAs must retire before the tensor memory is released
+      mma_commit(&h->mma_done);
+      mbar_wait(&h->mma_done, 0, a.err, nullptr, kSite + 5);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;   // token row within the tile
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++lt) {
+      const uint32_t acc = lt & 1u;
+      if (!mbar_wait(&h->acc_full[acc], (lt >> 1) & 1u, a.err, abort_flag, kSite + 6)) break;
+      tc_fence_after();
+      const int64_t t = (int64_t)tile * kBM + row;
+      const bool valid = t < a.T;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * a.Epad;
+      uint32_t r[16];
+      // pass 1: logits (+bias), running max
+      float m = -INFINITY;
+      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+        tmem_ld16(taddr + c0, r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = c0 + i;
+          if (e < a.E) {
+            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
+            m = fmaxf(m, l);
+            if (a.logits && valid) a.logits[t * a.E + e] = l;
+          }
+        }
+      }
+      // pass 2: sum of exp(l - max), sequential over experts
+      float sum = 0.0f;
+      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+        tmem_ld16(taddr + c0, r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = c0 + i;
+          if (e < a.E) {
+            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
+            sum = __fadd_rn(sum, softmax_exp(__fsub_rn(l, m)));
+          }
+        }
+      }
+      const float inv = __frcp_rn(sum);
+      // pass 3: probabilities and top-k
+      float tv[KMAX];
+      int ti[KMAX];
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
+      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+        tmem_ld16(taddr + c0, r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = c0 + i;
+          if (e < a.E) {
+            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
+            const float p = __fmul_rn(softmax_exp(__fsub_rn(l, m)), inv);
+            topk_insert<KMAX>(tv, ti, p, e);
+          }
+        }
+      }
+      // the accumulator can be reused by the MMA warp
+      tc_fence_before();
+      mbar_arrive(&h->acc_empty[acc]);
+      float ssum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (j < a.k) ssum = __fadd_rn(ssum, tv[j]);
+      const float invs = __frcp_rn(ssum);
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < KMAX; ++j) {
+          if (j < a.k) {
+            const float w = __fmul_rn(tv[j], invs);
+            a.ids[t * a.k + j] = ti[j];
+            if (a.weights) a.weights[t * a.k + j] = w;
+            if (a.weights_bf16) a.weights_bf16[t * a.k + j] = __float2bfloat16_rn(w);
+            if (a.do_perm) atomicOr(&h->bits[ti[j] * 4 + (row >> 5)], 1u << (row & 31));
+          }
+        }
+      }
+      if (a.do_perm) {
+        named_bar_sync(1, 128);
+        for (int e = row; e < a.E; e += 128) {
+          uint32_t b[4];
+          int cnt = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            b[i] = h->bits[e * 4 + i];
+            cnt += __popc(b[i]);
+            h->bits[e * 4 + i] = 0u;
+          }
+          a.tile_counts[(int64_t)tile * a.E + e] = cnt;
+          uint4 bv = make_uint4(b[0], b[1], b[2], b[3]);
+          reinterpret_cast<uint4*>(a.tile_bits)[(int64_t)tile * a.E + e] = bv;
+        }
+        named_bar_sync(1, 128);
+      }
+    }
+  }
+
+  __syncthreads();
+
+  // ---------------------------------------------------------------- permutation phase
+  if (a.do_perm) {
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(a.grid_sync, 1u);
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_gpu(a.grid_sync) < gridDim.x) {
+        if (((++spins) & 255u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+          report_error(a.err, kErrTimeout, kSite + 7);
+          h->abort = 1;
+          break;
+        }
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    if (!*abort_flag) {
+      // per-expert totals and, for each tile owned by this CTA, the count of earlier tiles
+      int32_t* pref = reinterpret_cast<int32_t*>(base);  // [own tiles, E] in the stage area
+      for (int e = tid; e < a.E; e += kThreads) {
+        int32_t run = 0;
+        for (int tile = 0; tile < a.num_tiles; ++tile) {
+          if ((tile % (int)gridDim.x) == (int)blockIdx.x) pref[(tile / gridDim.x) * a.E + e] = run;
+          run += __ldcg(&a.tile_counts[(int64_t)tile * a.E + e]);
+        }
+        h->total[e] = run;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int32_t off = 0;
+        for (int e = 0; e < a.E; ++e) {
+          h->offs[e] = off;
+          off += h->total[e];
+        }
+        h->offs[a.E] = off;
+      }
+      __syncthreads();
+      if (blockIdx.x == 0) {
+        for (int e = tid; e < a.E; e += kThreads) {
+          a.counts[e] = h->total[e];
+          a.offsets[e] = h->offs[e];
+        }
+        if (tid == 0) a.offsets[a.E] = h->offs[a.E];
+      }
+      int own = 0;
+      for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++own) {
+        for (int row = tid; row < kBM; row += kThreads) {
+          const int64_t t = (int64_t)tile * kBM + row;
+          if (t >= a.T) continue;
+          const int w = row >> 5;
+          const uint32_t below = (1u << (row & 31)) - 1u;
+          for (int j = 0; j < a.k; ++j) {
+            const int e = a.ids[t * a.k + j];
+            const uint4 bv = __ldcg(reinterpret_cast<const uint4*>(a.tile_bits) + (int64_t)tile * a.E + e);
+            const uint32_t b[4] = {bv.x, bv.y, bv.z, bv.w};
+            int rank = __popc(b[w] & below);
+            for (int i = 0; i < w; ++i) rank += __popc(b[i]);
+            const int32_t pos = h->offs[e] + pref[own * a.E + e] + rank;
+            a.sorted_idx[pos] = (int32_t)(t * a.k + j);
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+template <int KMAX>
+int launch_router(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const RouterArgs& a, int grid, size_t smem,
+                  cudaStream_t stream) {
+  auto fn = router_kernel<KMAX>;
+  LMOE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = a.do_perm ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, fn, tm_x, tm_w, a));
+}
+
+}  // namespace
+}  // namespace lmoe
+
+using namespace lmoe;
+
+extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts) {
+  if (num_tokens < 0 || num_experts <= 0) return 0;
+  const int64_t tiles = (num_tokens + kBM - 1) / kBM;
+  size_t bytes = 256;                                   // error word + grid barrier counter
+  bytes += (size_t)tiles * num_experts * sizeof(int32_t);
+  bytes = (bytes + 255) & ~size_t(255);
+  bytes += (size_t)tiles * num_experts * 4 * sizeof(uint32_t);
+  return bytes;
+}
+
+extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
+                                    int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                                    int32_t* ids, float* weights, void* weights_bf16, int32_t* counts,
+                                    int32_t* offsets, int32_t* sorted_idx, float* logits, void* workspace,
+                                    size_t workspace_bytes, lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(num_tokens >= 0 && num_tokens <= (int64_t)INT32_MAX / 16);
+  LMOE_ARG_CHECK(num_experts >= 1 && num_experts <= kMaxExperts);
+  LMOE_ARG_CHECK(top_k >= 1 && top_k <= 16 && top_k <= num_experts);
+  LMOE_ARG_CHECK(hidden_size >= kBK && hidden_size % kBK == 0);
+  LMOE_ARG_CHECK(ids != nullptr);
+  const bool do_perm = counts || offsets || sorted_idx;
+  if (do_perm) LMOE_ARG_CHECK(counts && offsets && sorted_idx);
+  if (num_tokens == 0) {
+    if (do_perm) {
+      LMOE_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * num_experts, stream));
+      LMOE_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (num_experts + 1), stream));
+    }
+    return LMOE_OK;
+  }
+  LMOE_ARG_CHECK(hidden && gate_weight && aligned16(hidden) && aligned16(gate_weight));
+  const size_t need = lmoe_router_workspace_bytes(num_tokens, num_experts);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
+
+  DeviceInfo dev;
+  int st = get_device_info(&dev);
+  if (st != LMOE_OK) return st;
+  if (dev.cc_major != 10) return LMOE_ERR_DEVICE;
+
+  const int E = num_experts;
+  const int Epad = ((E + 15) / 16) * 16;
+  const int num_tiles = (int)((num_tokens + kBM - 1) / kBM);
+  const uint32_t stage_bytes = kBM * kBK * 2 + Epad * kBK * 2;
+  const size_t hdr = (sizeof(RouterHdr) + 1023) & ~size_t(1023);
+  int stages = (int)((dev.max_smem_optin - hdr - 1024) / stage_bytes);
+  stages = stages > kMaxStages ? kMaxStages : stages;
+  if (stages < 2) return LMOE_ERR_UNSUPPORTED;
+  const size_t smem = 1024 + (size_t)stages * stage_bytes + sizeof(RouterHdr);
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < (uint32_t)(2 * Epad)) tmem_cols <<= 1;
+  const int grid = num_tiles < dev.num_sms ? num_tiles : dev.num_sms;
+  if (do_perm) {
+    const int own_max = (num_tiles + grid - 1) / grid;
+    if ((size_t)own_max * E * sizeof(int32_t) > (size_t)stages * stage_bytes) return LMOE_ERR_UNSUPPORTED;
+  }
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  LMOE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, stream));
+  RouterArgs a;
+  a.bias = gate_bias;
+  a.ids = ids;
+  a.weights = weights;
+  a.weights_bf16 = static_cast<__nv_bfloat16*>(weights_bf16);
+  a.logits = logits;
+  a.counts = counts;
+  a.offsets = offsets;
+  a.sorted_idx = sorted_idx;
+  a.err = reinterpret_cast<uint32_t*>(ws);
+  a.grid_sync = reinterpret_cast<uint32_t*>(ws) + 1;
+  a.tile_counts = reinterpret_cast<int32_t*>(ws + 256);
+  size_t tb_off = 256 + (size_t)num_tiles * E * sizeof(int32_t);
+  tb_off = (tb_off + 255) & ~size_t(255);
+  a.tile_bits = reinterpret_cast<uint32_t*>(ws + tb_off);
+  a.T = (int)num_tokens;
+  a.d = hidden_size;
+  a.E = E;
+  a.Epad = Epad;
+  a.k = top_k;
+  a.num_tiles = num_tiles;
+  a.stages = stages;
+  a.stage_bytes = stage_bytes;
+  a.tmem_cols = tmem_cols;
+  a.do_perm = do_perm ? 1 : 0;
+
+  CUtensorMap tm_x, tm_w;
+  st = encode_tmap_2d(&tm_x, hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)num_tokens,
+                      (uint64_t)hidden_size, (uint64_t)hidden_size * 2, kBM, kBK, true);
+  if (st != LMOE_OK) return st;
+  st = encode_tmap_2d(&tm_w, gate_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E, (uint64_t)hidden_size,
+                      (uint64_t)hidden_size * 2, (uint32_t)Epad, kBK, true);
+  if (st != LMOE_OK) return st;
+
+  if (top_k <= 2) return launch_router<2>(tm_x, tm_w, a, grid, smem, stream);
+  if (top_k <= 4) return launch_router<4>(tm_x, tm_w, a, grid, smem, stream);
+  if (top_k <= 8) return launch_router<8>(tm_x, tm_w, a, grid, smem, stream);
+  return launch_router<16>(tm_x, tm_w, a, grid, smem, stream);
+}

@@ -1,0 +1,141 @@
+"""GPU parity of the fused router (lmoe_fused_gate_topk) against the CPU oracle.
+
+Parity scheme (logit accumulation order on the tensor core differs from any CPU GEMM):
+  (i)   given the kernel's own fp32 logits, ids / weights / counts / offsets / sorted_idx
+        are bit-identical to the oracle's restatement of the reference routing;
+  (ii)  the logits agree with an fp64 oracle within the fp32 accumulation bound;
+  (iii) end to end, every token whose k-th / (k+1)-th logit gap exceeds twice that bound
+        gets exactly the oracle's experts.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import router
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(T, d, E, seed, wscale=0.02):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, d, generator=g) * wscale).to(torch.bfloat16)
+    return x.cuda(), w.cuda()
+
+
+def _check_given_logits(out, k, E):
+    ids, w = oracle.route(out["logits"], k)
+    assert np.array_equal(out["ids"], ids)
+    assert np.array_equal(out["weights"].view(np.uint32), w.view(np.uint32)), "weights not bit-exact"
+    assert np.array_equal(out["weights_bf16"], oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(w)))
+    counts, offsets, sidx = oracle.counts_offsets(ids, E)
+    assert np.array_equal(out["counts"], counts)
+    assert np.array_equal(out["offsets"], offsets)
+    assert np.array_equal(out["sorted_idx"], sidx)
+
+
+def _logit_bound(x, w):
+    ax = np.abs(x.float().cpu().numpy().astype(np.float64))
+    aw = np.abs(w.float().cpu().numpy().astype(np.float64))
+    return (ax @ aw.T) * 2.0 ** -18 + 1e-30
+
+
+@pytest.mark.parametrize("T,d,E,k", [(1, 64, 8, 2), (64, 4096, 8, 2), (257, 128, 16, 4), (300, 256, 64, 6),
+                                     (1000, 512, 8, 1), (129, 64, 256, 16), (77, 192, 40, 7), (512, 1024, 64, 8)])
+def test_router_bitexact_given_logits(T, d, E, k):
+    x, w = _inputs(T, d, E, seed=T + E)
+    out = router(x, w, k)
+    _check_given_logits(out, k, E)
+    # reference test_ops.py:116-141 properties
+    np.testing.assert_allclose(out["weights"].sum(1), np.ones(T), atol=1e-5)
+    assert out["ids"].min() >= 0 and out["ids"].max() < E
+
+
+@pytest.mark.parametrize("T,d,E,k", [(257, 128, 16, 4), (512, 4096, 64, 6), (1024, 2048, 8, 2)])
+def test_router_logits_and_end_to_end_ids(T, d, E, k):
+    x, w = _inputs(T, d, E, seed=7 * T + E)
+    out = router(x, w, k)
+    lg64 = oracle.gate_logits_f64(x.float().cpu().numpy(), w.float().cpu().numpy())
+    bound = _logit_bound(x, w)
+    assert np.all(np.abs(out["logits"] - lg64) <= bound), np.max(np.abs(out["logits"] - lg64) / bound)
+    # end-to-end: tokens whose selection margin exceeds 2x the bound must agree exactly
+    ids_ref, _ = oracle.route(lg64.astype(np.float32), k)
+    srt = np.sort(lg64, axis=1)[:, ::-1]
+    if k < E:
+        margin = srt[:, k - 1] - srt[:, k]
+        safe = margin > 2 * bound.max(axis=1)
+    else:
+        safe = np.ones(T, bool)
+    assert safe.mean() > 0.95
+    assert np.array_equal(np.sort(out["ids"][safe], 1), np.sort(ids_ref[safe], 1))
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (64, 6)])
+def test_router_full_size(E, k):
+    """Router workload: hidden [16384, 4096] bf16, N(0,1); router N(0, 0.02)."""
+    x, w = _inputs(16384, 4096, E, seed=E)
+    out = router(x, w, k)
+    _check_given_logits(out, k, E)
+    assert out["offsets"][-1] == 16384 * k
+
+
+def test_router_ties_go_to_lower_expert_id():
+    T, d, E, k = 200, 128, 16, 3
+    x, w = _inputs(T, d, E, seed=3)
+    w[9] = w[2]    # identical rows -> bit-identical logits
+    w[11] = w[2]
+    w[5] = w[14]
+    out = router(x, w, k)
+    _check_given_logits(out, k, E)
+    lg = out["logits"]
+    assert np.array_equal(lg[:, 9], lg[:, 2]) and np.array_equal(lg[:, 11], lg[:, 2])
+    for t in range(T):
+        sel = list(out["ids"][t])
+        if 9 in sel or 11 in sel:
+            assert 2 in sel and sel.index(2) < sel.index(9 if 9 in sel else 11)
+    # all-equal logits: ids 0..k-1
+    x0 = torch.zeros(4, d, dtype=torch.bfloat16, device="cuda")
+    out0 = router(x0, w, k)
+    assert out0["ids"].tolist() == [[0, 1, 2]] * 4
+
+
+def test_router_bias():
+    T, d, E, k = 333, 256, 64, 6
+    x, w = _inputs(T, d, E, seed=11)
+    b = torch.linspace(-2, 2, E, device="cuda", dtype=torch.float32)
+    out = router(x, w, k, bias=b)
+    _check_given_logits(out, k, E)
+    out_nb = router(x, w, k)
+    np.testing.assert_array_equal(out["logits"], (out_nb["logits"] + b.cpu().numpy()[None, :]).astype(np.float32))
+
+
+def test_router_without_permutation_outputs():
+    x, w = _inputs(100, 128, 8, seed=5)
+    a = router(x, w, 2, perm=False, logits=False)
+    b = router(x, w, 2)
+    assert np.array_equal(a["ids"], b["ids"]) and np.array_equal(a["weights"], b["weights"])
+
+
+def test_router_empty_batch():
+    x = torch.empty(0, 128, dtype=torch.bfloat16, device="cuda")
+    w = torch.randn(8, 128, device="cuda").to(torch.bfloat16)
+    out = router(x, w, 2, logits=False)
+    assert out["counts"].tolist() == [0] * 8 and out["offsets"].tolist() == [0] * 9
+
+
+def test_reference_surface_ops():
+    """light_moe._C-compatible ops: fused_gate_topk / fused_gate_topk_permute."""
+    from light_moe_b200 import ops
+    x, w = _inputs(300, 256, 8, seed=17)
+    ids, wts = ops.fused_gate_topk(x, w, 2)
+    assert ids.dtype == torch.int32 and wts.dtype == torch.bfloat16 and ids.shape == (300, 2)
+    torch.testing.assert_close(wts.float().sum(-1), torch.ones(300, device="cuda"), atol=1e-2, rtol=0)
+    perm, ids2, w2, offs, sidx = ops.fused_gate_topk_permute(x, w, 2)
+    assert torch.equal(ids, ids2) and offs.dtype == torch.int64 and sidx.dtype == torch.int64
+    assert perm.shape == (600, 256)
+    assert torch.equal(perm, x[sidx // 2])
+    counts, offsets, sidx_o = oracle.counts_offsets(ids.cpu().numpy(), 8)
+    assert np.array_equal(offs.cpu().numpy(), offsets) and np.array_equal(sidx.cpu().numpy(), sidx_o)
+    with pytest.raises(RuntimeError):
+        ops.fused_gate_topk(x.cpu(), w.cpu(), 2)
