@@ -1,0 +1,385 @@
+"""Benchmark: W4A16 MoE-layer tokens/s on B200 (Mixtral-8x7B expert shapes).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: expert parallel over NCCL)
+
+Workload (one "step" = one forward of the MoE layer over one batch):
+  d=4096, ffn=14336, 8 SwiGLU experts, top-2, int4 weights (symmetric, group 128, fp16
+  scales) quantised from N(0, 0.02); router N(0, 0.02) bf16; x ~ N(0, 1) bf16; seeded.
+  Headline: prefill, 8192 tokens per GPU.  A decode sub-measurement (64 tokens per GPU)
+  is reported under "decode".
+Timing: CUDA events on the launching stream, barrier + synchronize on both sides, max over
+ranks.  The int4 weights (727 MB) exceed the 126 MB L2, so every step streams them from HBM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, FFN, E, TOPK, GROUP = 4096, 14336, 8, 2, 128
+T_PREFILL, T_DECODE = 8192, 64
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"lmoe_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- problem
+def make_problem(T, device, seed=0):
+    import torch
+    from light_moe_b200.layer import W4A16Experts
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    gw = (torch.randn(E, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    # quantise expert by expert to bound the transient bf16 footprint
+    q1s, s1s, q3s, s3s, q2s, s2s = [], [], [], [], [], []
+    from light_moe_b200 import ops
+    for e in range(E):
+        w1 = (torch.randn(FFN, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        w3 = (torch.randn(FFN, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(D, FFN, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        for (w, qs, ss) in ((w1, q1s, s1s), (w3, q3s, s3s), (w2, q2s, s2s)):
+            q, s = ops.quantize_w4(w, GROUP)
+            qs.append(q)
+            ss.append(s)
+        del w1, w3, w2
+    st = torch.stack
+    ex = W4A16Experts.from_quantized(st(q1s), st(s1s), st(q3s), st(s3s), st(q2s), st(s2s), E, GROUP,
+                                     keep_canonical=True)
+    gx = torch.Generator(device=device).manual_seed(seed + 1)
+    x = torch.randn(T, D, generator=gx, device=device).to(torch.bfloat16)
+    return x, gw, ex
+
+
+# ----------------------------------------------------------------------------- timing helpers
+def time_device(fn, steps, warmup, stream, barrier=None):
+    import torch
+    for _ in range(warmup):
+        fn()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        fn()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    return ev0.elapsed_time(ev1) / 1e3  # seconds
+
+
+def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
+    """Time the dominant kernel (gate/up W4A16 GEMM, SwiGLU epilogue) alone on its stream."""
+    import torch
+    from light_moe_b200 import ops
+
+    ids, wts, counts, offsets, sidx = ops.fused_gate_topk_ex(x, gw, TOPK)[:5]
+    xp = x[(sidx // TOPK).long()].contiguous()
+    R = T * TOPK
+
+    def run():
+        return ops.w4a16_grouped_gemm(xp, ex.w13_packed, ex.w13_scales, offsets, E, 2 * FFN, GROUP, 1, None,
+                                      None, 0, T)
+
+    launches = 20
+    secs = time_device(run, launches, 3, stream) / launches
+    flops = 2.0 * R * (2 * FFN) * D
+    bytes_ = ex.w13_packed.numel() + ex.w13_scales.numel() * 2 + R * D * 2 + R * FFN * 2
+    if T >= 1024:
+        achieved = flops / secs / 1e12
+        peak = peaks["bf16_tflops"]
+        return {"kernel": "grouped_gemm_kernel<192,...,W4> gate/up+SwiGLU", "bound": "tensor",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} bf16 burst", "launch_us": round(secs * 1e6, 1),
+                "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
+    achieved = bytes_ / secs / 1e9
+    peak = peaks["hbm_gbs"]
+    return {"kernel": "grouped_gemm_kernel<64,...,W4> gate/up+SwiGLU", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_kind} HBM copy", "launch_us": round(secs * 1e6, 1),
+            "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
+
+
+# ----------------------------------------------------------------------------- CPU oracle baseline
+def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
+    """The oracle's numpy restatement of SparseMoEBlock on the dequantised weights."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from light_moe_b200 import ops
+
+    c = ex.canonical
+    w1 = ops.dequantize_w4(c["q1"], c["s1"], GROUP).float().cpu().numpy()
+    w3 = ops.dequantize_w4(c["q3"], c["s3"], GROUP).float().cpu().numpy()
+    w2 = ops.dequantize_w4(c["q2"], c["s2"], GROUP).float().cpu().numpy()
+    gwn = gw.float().cpu().numpy()
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((tokens, D), dtype=np.float32)
+    oracle.moe_layer_ref(x[:8], gwn, w1, w3, w2, TOPK)  # warm-up
+    done, t0 = 0, time.perf_counter()
+    reps = 0
+    while True:
+        oracle.moe_layer_ref(x, gwn, w1, w3, w2, TOPK)
+        done += tokens
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > seconds_budget or reps >= 3:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count()
+    return done / el, threads, f"{reps} x {tokens} tokens through the fp32 numpy SparseMoEBlock restatement"
+
+
+# ----------------------------------------------------------------------------- arms
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        barrier = dist.barrier
+    else:
+        barrier = None
+    peaks, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream()
+    from light_moe_b200 import ops
+    from light_moe_b200.layer import W4A16MoELayer
+
+    T = args.tokens
+    x, gw, ex = make_problem(T, device, seed=0)
+    if ws > 1:
+        from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
+        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None)
+        fwd = layer.forward
+        launches_per_step = layer.kernels_per_step
+    else:
+        layer = W4A16MoELayer(gw, ex, TOPK)
+        fwd = layer.forward
+        launches_per_step = 6   # router, table, gather, gate/up GEMM, down GEMM, combine
+
+    def step():
+        return fwd(x)
+
+    with ClockSampler(local) as clk:
+        secs = time_device(step, args.steps, args.warmup, stream, barrier)
+    # max over ranks
+    t = torch.tensor([secs], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = t.item()
+    value = T * ws * args.steps / secs
+
+    # end to end through the public API: pinned host x -> device, layer, y -> pinned host
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+
+    def e2e_step():
+        xd = xh.to(device, non_blocking=True)
+        y = fwd(xd)
+        yh.copy_(y, non_blocking=True)
+
+    esecs = time_device(e2e_step, args.steps, args.warmup, stream, barrier)
+    te = torch.tensor([esecs], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = T * ws * args.steps / te.item()
+
+    result = None
+    if rank == 0:
+        roof = gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind)
+        # decode sub-measurement (64 tokens per GPU)
+        xd = x[:T_DECODE].contiguous()
+        if ws > 1:
+            dsecs = None
+        else:
+            dsecs = time_device(lambda: fwd(xd), max(args.steps, 20), args.warmup, stream)
+        decode = None
+        if dsecs is not None:
+            dsteps = max(args.steps, 20)
+            droof = gemm_roofline(xd, gw, ex, T_DECODE, stream, peaks, peak_kind)
+            wbytes = (ex.w13_packed.numel() + ex.w13_scales.numel() * 2 + ex.w2_packed.numel()
+                      + ex.w2_scales.numel() * 2)
+            layer_gbs = wbytes / (dsecs / dsteps) / 1e9
+            decode = {"tokens": T_DECODE, "value": round(T_DECODE * dsteps / dsecs, 1), "unit": "tokens/s",
+                      "ms_per_step": round(dsecs / dsteps * 1e3, 4),
+                      "layer_weight_stream_gbs": round(layer_gbs, 1),
+                      "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4),
+                      "roofline_gate_up": droof}
+        cpu = None
+        if not args.no_cpu_baseline:
+            v, cores, sample = cpu_baseline(ex, gw, args.cpu_tokens)
+            cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        result = {
+            "metric": "W4A16 MoE-layer tokens/s (Mixtral-8x7B experts, prefill 8192 tokens/GPU)",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, int4 weights, fp32 accumulate",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights quantised to int4)",
+            "config": {"workload": "Mixtral-8x7B-shaped W4A16 MoE layer, prefill", "tokens_per_gpu": T,
+                       "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP,
+                       "parallelism": f"ep{ws}" if ws > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (727 MB int4 weights streamed every step)"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
+                    "d2h_bytes_per_step": T * D * 2},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": roof,
+            "decode": decode,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(result), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_reference(args):
+    """CPU arm: the oracle's fp32 numpy restatement of light-moe's SparseMoEBlock."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    import numpy as np
+
+    import oracle
+
+    tokens = args.cpu_tokens
+    rng = np.random.default_rng(0)
+    gw = (rng.standard_normal((E, D), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    # fp32 expert weights of the layer's shapes (the CPU path runs on dequantised int4 values;
+    # the values do not change its work, so they are drawn directly)
+    w = {name: (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+         for name, shape in (("w1", (E, FFN, D)), ("w3", (E, FFN, D)), ("w2", (E, D, FFN)))}
+    x = rng.standard_normal((tokens, D), dtype=np.float32)
+    for _ in range(args.warmup):
+        oracle.moe_layer_ref(x, gw, w["w1"], w["w3"], w["w2"], TOPK)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.moe_layer_ref(x, gw, w["w1"], w["w3"], w["w2"], TOPK)
+    el = time.perf_counter() - t0
+    value = tokens * args.steps / el
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count()
+    res = {"impl": "reference", "metric": "W4A16 MoE-layer tokens/s (Mixtral-8x7B experts, prefill 8192 tokens/GPU)",
+           "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp32 (dequantised int4 weights)", "data": "synthetic",
+           "config": {"workload": "Mixtral-8x7B-shaped W4A16 MoE layer, prefill", "tokens_per_step": tokens,
+                      "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP},
+           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"{tokens} tokens per step (bounded sample of the 8192-token batch)"},
+           "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=T_PREFILL)
+    ap.add_argument("--cpu-tokens", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

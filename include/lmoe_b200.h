@@ -65,13 +65,16 @@ size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts);
  *   offsets      int32 [num_experts + 1]  exclusive scan of counts        (optional*)
  *   sorted_idx   int32 [num_tokens*top_k]  flat index t*top_k+j ordered by
  *                (expert, token, slot)                                    (optional*)
+ *   positions    int32 [num_tokens*top_k]  inverse of sorted_idx: the sorted row of
+ *                each flat index (optional; needs the three outputs above)
  *   logits       fp32  [num_tokens, num_experts]  gate logits (+bias), for checking
  * (*) counts, offsets and sorted_idx are produced together: pass all three or none.
  */
 int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
                          int64_t num_tokens, int hidden_size, int num_experts, int top_k,
                          int32_t* ids, float* weights, void* weights_bf16,
-                         int32_t* counts, int32_t* offsets, int32_t* sorted_idx, float* logits,
+                         int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
+                         int32_t* positions, float* logits,
                          void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
 
 /* ------------------------------------------------------------------------------------ */
@@ -137,6 +140,8 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
  * epilogue 1: SwiGLU over a paired gate/up matrix of N = 2*F rows:
  *             output[r, f] = silu(gate[r, f]) * up[r, f]         (ldo >= F)
  * epilogue 2: output[dest_rows[r], n] = row_scale[r] * acc       (NULL = identity / 1)
+ * segment_expert: weight matrix used by each of the num_experts row segments (NULL: the
+ *             identity), so rows grouped by (source, expert) need no re-sort.
  * max_rows_per_expert: an upper bound of any expert's row count if known (0 = unknown);
  * small bounds select the decode-sized tiles.
  * New op; the reference has no W4A16 GEMM (SparseMoEBlockFast's GroupedLinear calls,
@@ -144,9 +149,21 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
 int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
                             const uint16_t* packed_scales, int N, int group_size,
                             const void* expert_offsets, int offsets_are_int64, int num_experts,
+                            const int32_t* segment_expert,
                             int epilogue, const int32_t* dest_rows, const float* row_scale,
                             int64_t max_rows_per_expert, void* output, int64_t ldo,
                             void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
+
+/* Weighted combine of per-slot expert rows back to tokens:
+ *   y[t, :] = sum_j weights[t*top_k+j] * rows[positions[t*top_k+j], :]
+ *             + sum_s extra_rows[s*num_tokens + t, :]
+ * fp32 accumulation in slot order, bf16 in / out, hidden_size even.
+ * Replaces unpermute_tokens (python/light_moe/ops/grouped_gemm.py:250-279) and the
+ * expert-parallel unsort + weighted sum (python/light_moe/distributed/expert_parallel.py:
+ * 307-317). */
+int lmoe_combine_rows(const void* rows, const int32_t* positions, const float* weights,
+                      int64_t num_tokens, int top_k, int hidden_size,
+                      const void* extra_rows, int num_extra, void* y, lmoe_stream_t stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* The W4A16 MoE layer: router -> gather -> gate/up GEMM (SwiGLU) -> down GEMM (routing   */

@@ -35,7 +35,7 @@ torch::Tensor workspace(int64_t bytes, const torch::Tensor& like) {
 }
 
 struct Routed {
-  torch::Tensor ids, weights, counts, offsets, sorted_idx, logits;
+  torch::Tensor ids, weights, counts, offsets, sorted_idx, positions, logits;
 };
 
 Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weight,
@@ -64,6 +64,7 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
     r.counts = torch::empty({E}, i32);
     r.offsets = torch::empty({E + 1}, i32);
     r.sorted_idx = torch::empty({T * top_k}, i32);
+    r.positions = torch::empty({T * top_k}, i32);
   }
   if (want_logits) r.logits = torch::empty({T, E}, x.options().dtype(torch::kFloat32));
   auto ws = workspace((int64_t)lmoe_router_workspace_bytes(T, (int)E), x);
@@ -72,6 +73,7 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
                                 perm ? r.counts.data_ptr<int32_t>() : nullptr,
                                 perm ? r.offsets.data_ptr<int32_t>() : nullptr,
                                 perm ? r.sorted_idx.data_ptr<int32_t>() : nullptr,
+                                perm ? r.positions.data_ptr<int32_t>() : nullptr,
                                 want_logits ? r.logits.data_ptr<float>() : nullptr, ws.data_ptr(), ws.numel(),
                                 cur_stream());
   check_status(st, "fused_gate_topk");
@@ -132,7 +134,7 @@ torch::Tensor grouped_gemm(torch::Tensor input, torch::Tensor weights, torch::Te
 std::vector<torch::Tensor> fused_gate_topk_ex(torch::Tensor hidden_states, torch::Tensor gate_weight, int64_t top_k,
                                               std::optional<torch::Tensor> bias, bool return_logits) {
   Routed r = route(hidden_states, gate_weight, bias, top_k, true, return_logits);
-  std::vector<torch::Tensor> out = {r.ids, r.weights, r.counts, r.offsets, r.sorted_idx};
+  std::vector<torch::Tensor> out = {r.ids, r.weights, r.counts, r.offsets, r.sorted_idx, r.positions};
   if (return_logits) out.push_back(r.logits);
   return out;
 }
@@ -211,7 +213,7 @@ torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torc
                                  torch::Tensor expert_offsets, int64_t num_experts, int64_t N, int64_t group_size,
                                  int64_t epilogue, std::optional<torch::Tensor> dest_rows,
                                  std::optional<torch::Tensor> row_scale, int64_t out_rows,
-                                 int64_t max_rows_per_expert) {
+                                 int64_t max_rows_per_expert, std::optional<torch::Tensor> segment_expert) {
   check_cuda(input, "input");
   check_cuda(packed, "packed");
   const c10::cuda::OptionalCUDAGuard guard(input.device());
@@ -224,14 +226,34 @@ torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torc
   torch::Tensor dr, rs;
   if (dest_rows.has_value() && dest_rows->defined()) dr = dest_rows->to(torch::kInt32).contiguous();
   if (row_scale.has_value() && row_scale->defined()) rs = row_scale->to(torch::kFloat32).contiguous();
+  torch::Tensor se;
+  if (segment_expert.has_value() && segment_expert->defined()) se = segment_expert->to(torch::kInt32).contiguous();
   auto ws = workspace((int64_t)lmoe_gemm_workspace_bytes(), x);
   int st = lmoe_w4a16_grouped_gemm(
       x.data_ptr(), T, (int)K, packed.data_ptr<uint8_t>(), reinterpret_cast<const uint16_t*>(packed_scales.data_ptr()),
       (int)N, (int)group_size, off.data_ptr(), off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts,
-      (int)epilogue, dr.defined() ? dr.data_ptr<int32_t>() : nullptr, rs.defined() ? rs.data_ptr<float>() : nullptr,
+      se.defined() ? se.data_ptr<int32_t>() : nullptr, (int)epilogue, dr.defined() ? dr.data_ptr<int32_t>() : nullptr, rs.defined() ? rs.data_ptr<float>() : nullptr,
       max_rows_per_expert, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), cur_stream());
   check_status(st, "w4a16_grouped_gemm");
   return out;
+}
+
+torch::Tensor combine_rows(torch::Tensor rows, torch::Tensor positions, torch::Tensor weights, int64_t num_tokens,
+                           int64_t top_k, std::optional<torch::Tensor> extra_rows, int64_t num_extra) {
+  check_cuda(rows, "rows");
+  const c10::cuda::OptionalCUDAGuard guard(rows.device());
+  auto r = as_bf16_contig(rows);
+  auto p = positions.to(torch::kInt32).contiguous();
+  auto w = weights.to(torch::kFloat32).contiguous();
+  const int64_t d = r.size(1);
+  torch::Tensor ex;
+  if (extra_rows.has_value() && extra_rows->defined()) ex = as_bf16_contig(*extra_rows);
+  auto y = torch::empty({num_tokens, d}, r.options());
+  int st = lmoe_combine_rows(r.data_ptr(), p.data_ptr<int32_t>(), w.data_ptr<float>(), num_tokens, (int)top_k, (int)d,
+                             ex.defined() ? ex.data_ptr() : nullptr, ex.defined() ? (int)num_extra : 0, y.data_ptr(),
+                             cur_stream());
+  check_status(st, "combine_rows");
+  return y;
 }
 
 std::vector<torch::Tensor> moe_layer_w4a16(torch::Tensor x, torch::Tensor gate_weight, torch::Tensor w13_packed,
@@ -284,7 +306,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm, "W4A16 grouped GEMM", py::arg("input"), py::arg("packed"),
         py::arg("packed_scales"), py::arg("expert_offsets"), py::arg("num_experts"), py::arg("N"),
         py::arg("group_size"), py::arg("epilogue") = 0, py::arg("dest_rows") = py::none(),
-        py::arg("row_scale") = py::none(), py::arg("out_rows") = 0, py::arg("max_rows_per_expert") = 0);
+        py::arg("row_scale") = py::none(), py::arg("out_rows") = 0, py::arg("max_rows_per_expert") = 0,
+        py::arg("segment_expert") = py::none());
+  m.def("combine_rows", &combine_rows, "Weighted combine of slot rows back to tokens", py::arg("rows"),
+        py::arg("positions"), py::arg("weights"), py::arg("num_tokens"), py::arg("top_k"),
+        py::arg("extra_rows") = py::none(), py::arg("num_extra") = 0);
   m.def("moe_layer_w4a16", &moe_layer_w4a16, "W4A16 MoE layer", py::arg("x"), py::arg("gate_weight"),
         py::arg("w13_packed"), py::arg("w13_scales"), py::arg("w2_packed"), py::arg("w2_scales"), py::arg("top_k"),
         py::arg("ffn_size"), py::arg("group_size"), py::arg("num_shared") = 0, py::arg("gate_bias") = py::none());

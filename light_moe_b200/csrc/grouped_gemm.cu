@@ -54,8 +54,9 @@ struct GemmArgs {
   int group_size;           // W4
   int G;                    // W4: K / group_size
   // problem
-  const void* offsets;      // [E+1]
+  const void* offsets;      // [E+1] row ranges of the segments
   int offsets_i64;
+  const int32_t* seg_expert; // weight matrix used by each segment (NULL: segment e uses expert e)
   int E, N, K, NB, KB;      // NB = ceil(N / 128) weight-row blocks, KB = K / 64
   int mode;
   __nv_bfloat16* out;
@@ -92,10 +93,11 @@ struct __align__(8) GemmBars {
   int total_tiles;
   int tile_start[kMaxGemmExperts + 1];
   int row_off[kMaxGemmExperts + 1];
+  int seg_w[kMaxGemmExperts];
 };
 
 struct TileInfo {
-  int e, fb, row0, rows;
+  int e, w, fb, row0, rows;   // segment, its weight matrix, feature block, first row, rows
 };
 
 // Tiles are numbered expert-major, then feature block, then token block (fastest).
@@ -109,6 +111,7 @@ __device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_
   const int local = tile - b->tile_start[e];
   TileInfo ti;
   ti.e = e;
+  ti.w = b->seg_w[e];
   ti.fb = local / ntb;
   const int tb = local - ti.fb * ntb;
   ti.row0 = b->row_off[e] + tb * BN;
@@ -155,14 +158,14 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
   if (tid == 0) {
     for (int s = 0; s < C::kWStages; ++s) {
       mbar_init(&bars->w_full[s], 1);
-      mbar_init(&bars->w_empty[s], W4 ? C::kDQWarps : 1);
+      mbar_init(&bars->w_empty[s], W4 ? 4 : 1);
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bars->b_full[s], 1);
       mbar_init(&bars->b_empty[s], 1);
     }
     for (int s = 0; s < AST; ++s) {
-      mbar_init(&bars->a_full[s], C::kDQWarps > 0 ? C::kDQWarps : 1);
+      mbar_init(&bars->a_full[s], W4 ? 4 : 1);
       mbar_init(&bars->a_empty[s], 1);
     }
     for (int s = 0; s < ACC; ++s) {
@@ -185,6 +188,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
   for (int e = tid; e <= a.E; e += C::kThreads) {
     bars->row_off[e] = a.offsets_i64 ? (int)static_cast<const int64_t*>(a.offsets)[e]
                                      : static_cast<const int32_t*>(a.offsets)[e];
+    if (e < a.E) bars->seg_w[e] = a.seg_expert ? a.seg_expert[e] : e;
   }
   __syncthreads();
   if (tid == 0) {
@@ -220,8 +224,8 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
         const uint8_t* wblk = nullptr;
         const uint16_t* sblk = nullptr;
         if (W4) {
-          wblk = a.wq + (size_t)(ti.e * a.NB + ti.fb) * KB * kW4BlockBytes;
-          sblk = a.wscale + (size_t)(ti.e * a.NB + ti.fb) * a.G * kBM;
+          wblk = a.wq + (size_t)(ti.w * a.NB + ti.fb) * KB * kW4BlockBytes;
+          sblk = a.wscale + (size_t)(ti.w * a.NB + ti.fb) * a.G * kBM;
         }
         for (int kb = 0; kb < KB; ++kb) {
           if (W4) {
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
           } else {
             mbar_arrive_expect_tx(&bars->b_full[s2], C::kBStageBytes + C::kAStageBytes);
             tma_load_2d(a_stages + s2 * C::kAStageBytes, &tm_w, &bars->b_full[s2], kb * kBK,
-                        ti.e * a.N + ti.fb * kBM);
+                        ti.w * a.N + ti.fb * kBM);
           }
           tma_load_2d(bsm, &tm_x, &bars->b_full[s2], kb * kBK, ti.row0);
           ++bit;
@@ -303,52 +307,53 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
     }
   } else if (W4 && warp < C::kEpiWarp0) {
     // ------------------------------------------------------------------ int4 dequantisers
-    const int dw = warp - 2;
+    // DQ / 4 groups of 4 warps (one warp per TMEM lane quarter, one weight row per thread).
+    // Group g owns every (DQ/4)-th k-block, so several k-blocks are dequantised at once and
+    // the barrier / shared-load / tensor-memory-store latency of one block overlaps the
+    // arithmetic of the others.
+    constexpr int kGroups = DQ / 4;
+    const int grp = (warp - 2) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    constexpr int kHalves = (DQ >= 8) ? 1 : 2;        // 16-byte halves handled per thread
-    const int half0 = (DQ >= 8) ? (dw >> 2) : 0;
     const __nv_bfloat162 off136 = __floats2bfloat162_rn(136.0f, 136.0f);
-    uint32_t wit = 0, ait = 0;
+    uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = wit % WST;
-        if (!mbar_wait(&bars->w_full[s], (wit / WST) & 1u, a.err, abort_flag, kSite + 10)) { ok = false; break; }
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        if ((int)(it % kGroups) != grp) continue;
+        const int s = it % WST;
+        if (!mbar_wait(&bars->w_full[s], (it / WST) & 1u, a.err, abort_flag, kSite + 10)) { ok = false; break; }
         const uint8_t* wsm = w_stages + s * C::kWStageBytes;
-        uint4 v[kHalves];
-#pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh)
-          v[hh] = *reinterpret_cast<const uint4*>(wsm + (half0 + hh) * 2048 + row * 16);
+        const uint4 v0 = *reinterpret_cast<const uint4*>(wsm + row * 16);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(wsm + 2048 + row * 16);
         const uint16_t sbits = reinterpret_cast<const uint16_t*>(wsm + kW4BlockBytes)[row];
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->w_empty[s]);
-        ++wit;
         // exact split of the fp16 scale into bf16 hi + lo parts
         const float sf = __half2float(__ushort_as_half(sbits));
         const __nv_bfloat16 shi = __float2bfloat16_rz(sf);
         const __nv_bfloat16 slo = __float2bfloat16_rn(__fsub_rn(sf, __bfloat162float(shi)));
         const __nv_bfloat162 s_hi = __nv_bfloat162(shi, shi);
         const __nv_bfloat162 s_lo = __nv_bfloat162(slo, slo);
-        uint32_t outv[kHalves][16];
-#pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh) {
-          dequant_word(v[hh].x, s_hi, s_lo, off136, &outv[hh][0]);
-          dequant_word(v[hh].y, s_hi, s_lo, off136, &outv[hh][4]);
-          dequant_word(v[hh].z, s_hi, s_lo, off136, &outv[hh][8]);
-          dequant_word(v[hh].w, s_hi, s_lo, off136, &outv[hh][12]);
-        }
-        const int as = ait % AST;
-        if (!mbar_wait(&bars->a_empty[as], ((ait / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
+        uint32_t o0[16], o1[16];
+        dequant_word(v0.x, s_hi, s_lo, off136, &o0[0]);
+        dequant_word(v0.y, s_hi, s_lo, off136, &o0[4]);
+        dequant_word(v0.z, s_hi, s_lo, off136, &o0[8]);
+        dequant_word(v0.w, s_hi, s_lo, off136, &o0[12]);
+        dequant_word(v1.x, s_hi, s_lo, off136, &o1[0]);
+        dequant_word(v1.y, s_hi, s_lo, off136, &o1[4]);
+        dequant_word(v1.z, s_hi, s_lo, off136, &o1[8]);
+        dequant_word(v1.w, s_hi, s_lo, off136, &o1[12]);
+        const int as = it % AST;
+        if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_a + ((uint32_t)(q * 32) << 16) + as * 32;
-#pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh) tmem_st16(taddr + (half0 + hh) * 16, outv[hh]);
+        tmem_st16(taddr, o0);
+        tmem_st16(taddr + 16, o1);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->a_full[as]);
-        ++ait;
       }
     }
   } else {
@@ -461,6 +466,7 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.G = w4 ? p.K / p.group_size : 0;
   a.offsets = p.offsets;
   a.offsets_i64 = p.offsets_i64;
+  a.seg_expert = p.seg_expert;
   a.E = p.num_experts;
   a.N = p.N;
   a.K = p.K;
@@ -488,8 +494,8 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   }
   const int grid = dev.num_sms;
   if (w4) {
-    if (small) return launch_gemm<64, 8, 16, 4, 8, 2, true>(tm_x, tm_w, a, grid, stream);
-    return launch_gemm<192, 8, 8, 4, 4, 2, true>(tm_x, tm_w, a, grid, stream);
+    if (small) return launch_gemm<64, 16, 16, 4, 8, 2, true>(tm_x, tm_w, a, grid, stream);
+    return launch_gemm<192, 12, 8, 4, 4, 2, true>(tm_x, tm_w, a, grid, stream);
   }
   if (small) return launch_gemm<64, 0, 1, 6, 1, 2, false>(tm_x, tm_w, a, grid, stream);
   return launch_gemm<192, 0, 1, 4, 1, 2, false>(tm_x, tm_w, a, grid, stream);

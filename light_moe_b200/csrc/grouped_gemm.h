@@ -23,7 +23,10 @@ struct GemmProblem {
   // expert row ranges [num_experts + 1] (int32, or int64 when offsets_i64)
   const void* offsets = nullptr;
   int offsets_i64 = 0;
-  int num_experts = 0;
+  int num_experts = 0;  // number of row segments
+  // weight matrix of each segment (NULL: segment e uses matrix e); lets rows that arrive
+  // grouped by (source rank, expert) be multiplied without a local re-sort
+  const int32_t* seg_expert = nullptr;
   // weights: either W4 prepacked (wq + wscale) or bf16 [num_experts, N, K] (w)
   const uint8_t* wq = nullptr;
   const uint16_t* wscale = nullptr;

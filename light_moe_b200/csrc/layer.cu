@@ -136,6 +136,30 @@ __global__ void combine_slots_kernel(const __nv_bfloat162* __restrict__ o, int64
   y[i] = __floats2bfloat162_rn(ax, ay);
 }
 
+// y[t, :] = sum_j w[t*k+j] * rows[pos[t*k+j], :] + sum_s extra[s*T + t, :]  (fp32, fixed order)
+__global__ void combine_rows_kernel(const __nv_bfloat162* __restrict__ rows, const int32_t* __restrict__ pos,
+                                    const float* __restrict__ w, int64_t T, int k, int d2,
+                                    const __nv_bfloat162* __restrict__ extra, int S,
+                                    __nv_bfloat162* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * d2) return;
+  const int64_t t = i / d2;
+  const int c = (int)(i - t * d2);
+  float ax = 0.0f, ay = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    const float wj = w[t * k + j];
+    const float2 v = __bfloat1622float2(rows[(int64_t)pos[t * k + j] * d2 + c]);
+    ax = __fadd_rn(ax, __fmul_rn(wj, v.x));
+    ay = __fadd_rn(ay, __fmul_rn(wj, v.y));
+  }
+  for (int s = 0; s < S; ++s) {
+    const float2 v = __bfloat1622float2(extra[((int64_t)s * T + t) * d2 + c]);
+    ax = __fadd_rn(ax, v.x);
+    ay = __fadd_rn(ay, v.y);
+  }
+  y[i] = __floats2bfloat162_rn(ax, ay);
+}
+
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Workspace carve-up of the layer (all 256-byte aligned).
@@ -241,7 +265,8 @@ extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int
 extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
                                        const uint16_t* packed_scales, int N, int group_size,
                                        const void* expert_offsets, int offsets_are_int64, int num_experts,
-                                       int epilogue, const int32_t* dest_rows, const float* row_scale,
+                                       const int32_t* segment_expert, int epilogue, const int32_t* dest_rows,
+                                       const float* row_scale,
                                        int64_t max_rows_per_expert, void* output, int64_t ldo, void* workspace,
                                        size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
@@ -260,6 +285,7 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
   p.offsets = expert_offsets;
   p.offsets_i64 = offsets_are_int64;
   p.num_experts = num_experts;
+  p.seg_expert = segment_expert;
   p.wq = packed;
   p.wscale = packed_scales;
   p.group_size = group_size;
@@ -272,6 +298,21 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
   p.err = static_cast<uint32_t*>(workspace);
   p.max_rows_per_expert_hint = max_rows_per_expert;
   return run_grouped_gemm(p, stream);
+}
+
+extern "C" int lmoe_combine_rows(const void* rows, const int32_t* positions, const float* weights, int64_t num_tokens,
+                                 int top_k, int hidden_size, const void* extra_rows, int num_extra, void* y,
+                                 lmoe_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(num_tokens >= 0 && top_k >= 0 && hidden_size > 0 && (hidden_size % 2) == 0 && num_extra >= 0);
+  if (num_tokens == 0) return LMOE_OK;
+  LMOE_ARG_CHECK(y && (top_k == 0 || (rows && positions && weights)) && (num_extra == 0 || extra_rows));
+  const int threads = 256;
+  const int64_t n = num_tokens * (hidden_size / 2);
+  combine_rows_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat162*>(rows), positions, weights, num_tokens, top_k, hidden_size / 2,
+      static_cast<const __nv_bfloat162*>(extra_rows), num_extra, static_cast<__nv_bfloat162*>(y));
+  return cuda_status(cudaGetLastError());
 }
 
 extern "C" size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int ffn_size, int num_experts,
@@ -312,7 +353,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   const int64_t R = T * k + (int64_t)S * T;
 
   int st = lmoe_fused_gate_topk(x, gate_weight, gate_bias, T, d, E, k, ids, wts, nullptr, counts, offs, sidx,
-                                nullptr, at(L.router), lmoe_router_workspace_bytes(T, E), stream_);
+                                nullptr, nullptr, at(L.router), lmoe_router_workspace_bytes(T, E), stream_);
   if (st != LMOE_OK) return st;
   {
     const int threads = 256;

@@ -47,6 +47,7 @@ struct RouterArgs {
   int32_t* counts;
   int32_t* offsets;
   int32_t* sorted_idx;
+  int32_t* positions;     // optional inverse of sorted_idx: positions[t*k+j] = its sorted row
   int32_t* tile_counts;   // [num_tiles, E]
   uint32_t* tile_bits;    // [num_tiles, E, 4] : bit r of word r/32 set if token row r picked e
   uint32_t* grid_sync;    // arrival counter for the grid barrier (zeroed by the host)
@@ -334,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < w; ++i) rank += __popc(b[i]);
             const int32_t pos = h->offs[e] + pref[own * a.E + e] + rank;
             a.sorted_idx[pos] = (int32_t)(t * a.k + j);
+            if (a.positions) a.positions[t * a.k + j] = pos;
           }
         }
       }
@@ -383,23 +385,26 @@ extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_expert
 extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
                                     int64_t num_tokens, int hidden_size, int num_experts, int top_k,
                                     int32_t* ids, float* weights, void* weights_bf16, int32_t* counts,
-                                    int32_t* offsets, int32_t* sorted_idx, float* logits, void* workspace,
+                                    int32_t* offsets, int32_t* sorted_idx, int32_t* positions, float* logits,
+                                    void* workspace,
                                     size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   LMOE_ARG_CHECK(num_tokens >= 0 && num_tokens <= (int64_t)INT32_MAX / 16);
   LMOE_ARG_CHECK(num_experts >= 1 && num_experts <= kMaxExperts);
   LMOE_ARG_CHECK(top_k >= 1 && top_k <= 16 && top_k <= num_experts);
   LMOE_ARG_CHECK(hidden_size >= kBK && hidden_size % kBK == 0);
-  LMOE_ARG_CHECK(ids != nullptr);
   const bool do_perm = counts || offsets || sorted_idx;
-  if (do_perm) LMOE_ARG_CHECK(counts && offsets && sorted_idx);
   if (num_tokens == 0) {
+    // ids / weights / sorted_idx are empty (possibly NULL); only counts and offsets exist
+    if (do_perm) LMOE_ARG_CHECK(counts && offsets);
     if (do_perm) {
       LMOE_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * num_experts, stream));
       LMOE_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (num_experts + 1), stream));
     }
     return LMOE_OK;
   }
+  LMOE_ARG_CHECK(ids != nullptr);
+  if (do_perm) LMOE_ARG_CHECK(counts && offsets && sorted_idx);
   LMOE_ARG_CHECK(hidden && gate_weight && aligned16(hidden) && aligned16(gate_weight));
   const size_t need = lmoe_router_workspace_bytes(num_tokens, num_experts);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
@@ -437,6 +442,7 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   a.counts = counts;
   a.offsets = offsets;
   a.sorted_idx = sorted_idx;
+  a.positions = do_perm ? positions : nullptr;
   a.err = reinterpret_cast<uint32_t*>(ws);
   a.grid_sync = reinterpret_cast<uint32_t*>(ws) + 1;
   a.tile_counts = reinterpret_cast<int32_t*>(ws + 256);

@@ -1,0 +1,235 @@
+"""Expert-parallel W4A16 MoE layer over NCCL (one process per GPU).
+
+Keeps the interface of light-moe's expert-parallel module
+(python/light_moe/distributed/expert_parallel.py:17-87: ``ExpertParallelConfig``,
+``ExpertParallelGroup``) and replaces its ``ExpertParallelMoELayer`` (:90-354), which pads
+to equal splits and applies local expert 0 to every token, with the real computation:
+
+  1. route the rank's own tokens (router kernel: ids, weights, counts, offsets, stable
+     sorted order and its inverse) -- tokens are data-parallel, the router is replicated;
+  2. gather the token rows in expert order; experts live in contiguous blocks per rank
+     (rank r owns [r*E/ep, (r+1)*E/ep), as at expert_parallel.py:120-121), so this order
+     is also destination-rank order;
+  3. exchange the per-(rank, expert) counts with one all-to-all and copy them to the host
+     (the only host synchronisation: NCCL needs the split sizes);
+  4. all-to-all-v dispatch of the bf16 rows;
+  5. the received rows are grouped by (source rank, local expert); the grouped GEMMs take
+     those segments directly, with a segment -> expert map, so no local re-sort is needed:
+     gate/up GEMM with the SwiGLU epilogue, then the down GEMM;
+  6. all-to-all-v combine back to the source ranks (same split sizes, reversed);
+  7. weighted combine into the token order with the inverse permutation (fp32, slot order);
+     always-on shared experts run locally on the rank's tokens in the same GEMM launches.
+
+The steps that move data between ranks use ``torch.distributed`` collectives, so the
+whole flow also runs with the gloo backend on CPU processes when a CPU expert backend is
+supplied (the tests do this); the product backend is the CUDA library.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from datetime import timedelta
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .layer import W4A16Experts
+
+
+@dataclass
+class ExpertParallelConfig:
+    """Configuration for expert parallelism (expert_parallel.py:17-30 of the reference)."""
+
+    num_experts: int = 8
+    top_k: int = 2
+    hidden_size: int = 4096
+    intermediate_size: int = 14336
+    ep_size: int = 8
+    group_size: int = 128
+    num_shared: int = 0
+
+    @property
+    def experts_per_rank(self) -> int:
+        assert self.num_experts % self.ep_size == 0, "num_experts must be divisible by ep_size"
+        return self.num_experts // self.ep_size
+
+
+class ExpertParallelGroup:
+    """The expert-parallel process group (expert_parallel.py:33-87 of the reference)."""
+
+    def __init__(self, ep_size: int = 8):
+        self.ep_size = ep_size
+        self.group: Optional[dist.ProcessGroup] = None
+        self.rank = 0
+        self.world_size = 1
+        self.initialized = False
+
+    def init_process_group(self, backend: str = "nccl", init_method: str = "env://", timeout_s: float = 120.0,
+                           device_id: Optional[torch.device] = None):
+        if not dist.is_initialized():
+            kw = dict(backend=backend, init_method=init_method, timeout=timedelta(seconds=timeout_s))
+            if device_id is not None:
+                kw["device_id"] = device_id
+            dist.init_process_group(**kw)
+        return self.attach()
+
+    def attach(self, group: Optional[dist.ProcessGroup] = None):
+        """Use an existing process group (default: the world)."""
+        self.world_size = dist.get_world_size()
+        self.rank = dist.get_rank()
+        if self.world_size < self.ep_size:
+            raise ValueError(f"world size {self.world_size} < EP size {self.ep_size}")
+        if group is None and self.ep_size != self.world_size:
+            group = dist.new_group(list(range(self.ep_size)))
+        self.group = group
+        self.initialized = True
+        return self
+
+    def all_to_all(self, output_tensor, input_tensor, output_split_sizes=None, input_split_sizes=None):
+        dist.all_to_all_single(output_tensor, input_tensor, output_split_sizes, input_split_sizes, group=self.group)
+        return output_tensor
+
+    def all_reduce(self, tensor):
+        dist.all_reduce(tensor, group=self.group)
+        return tensor
+
+
+class CudaExpertBackend:
+    """Local expert compute on the sm_100a library (the product path)."""
+
+    def __init__(self, local: W4A16Experts, top_k: int):
+        self.ex = local
+        self.top_k = top_k
+        self.num_local = local.num_experts      # routed experts on this rank
+        self.num_shared = local.num_shared
+
+    def route(self, x, gate_weight, gate_bias):
+        ids, w, counts, offsets, sidx, pos = ops.fused_gate_topk_ex(x, gate_weight, self.top_k, gate_bias)[:6]
+        return ids, w, counts, offsets, sidx, pos
+
+    def gather(self, x, sorted_idx):
+        from . import capi
+        rows = torch.empty(sorted_idx.numel(), x.shape[1], dtype=x.dtype, device=x.device)
+        capi.call("lmoe_permute_rows", x.data_ptr(), sorted_idx.data_ptr(), sorted_idx.numel(), x.shape[1],
+                  self.top_k, rows.data_ptr(), capi.stream_handle())
+        return rows
+
+    def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+        e = self.ex
+        h = ops.w4a16_grouped_gemm(rows, e.w13_packed, e.w13_scales, seg_offsets, num_seg, 2 * e.ffn_size,
+                                   e.group_size, 1, None, None, 0, max_rows, seg_expert)
+        return ops.w4a16_grouped_gemm(h, e.w2_packed, e.w2_scales, seg_offsets, num_seg, e.hidden_size,
+                                      e.group_size, 0, None, None, 0, max_rows, seg_expert)
+
+    def combine(self, rows, positions, weights, T, extra, num_extra):
+        return ops.combine_rows(rows, positions, weights, T, self.top_k, extra, num_extra)
+
+
+class ExpertParallelW4A16Layer(torch.nn.Module):
+    """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks."""
+
+    def __init__(self, config: ExpertParallelConfig, ep_group: ExpertParallelGroup, gate_weight: torch.Tensor,
+                 backend, gate_bias: Optional[torch.Tensor] = None):
+        super().__init__()
+        self.config = config
+        self.ep_group = ep_group
+        self.gate_weight = gate_weight
+        self.gate_bias = gate_bias
+        self.backend = backend
+        self.experts_per_rank = config.experts_per_rank
+        self.local_expert_start = ep_group.rank * self.experts_per_rank
+        self.local_expert_end = self.local_expert_start + self.experts_per_rank
+        # kernels of ours per forward: router, gather, gate/up GEMM, down GEMM, combine
+        self.kernels_per_step = 5
+        self._seg_cache = {}
+
+    @classmethod
+    def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
+                  group: Optional[dist.ProcessGroup] = None, gate_bias: Optional[torch.Tensor] = None):
+        """Build this rank's layer from the full (all-expert) prepacked weights."""
+        ws = dist.get_world_size(group)
+        g = ExpertParallelGroup(ws).attach(group)
+        cfg = ExpertParallelConfig(num_experts=experts.num_experts, top_k=top_k, hidden_size=experts.hidden_size,
+                                   intermediate_size=experts.ffn_size, ep_size=ws, group_size=experts.group_size,
+                                   num_shared=experts.num_shared)
+        local = slice_experts(experts, g.rank * cfg.experts_per_rank, (g.rank + 1) * cfg.experts_per_rank)
+        return cls(cfg, g, gate_weight.to(torch.bfloat16).contiguous(), CudaExpertBackend(local, top_k), gate_bias)
+
+    def _segments(self, device):
+        key = (str(device),)
+        if key not in self._seg_cache:
+            ep, epr, S = self.ep_group.ep_size, self.experts_per_rank, self.config.num_shared
+            seg = [i % epr for i in range(ep * epr)] + [epr + s for s in range(S)]
+            self._seg_cache[key] = torch.tensor(seg, dtype=torch.int32, device=device)
+        return self._seg_cache[key]
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        x = hidden_states.reshape(-1, hidden_states.shape[-1])
+        T, d = x.shape
+        cfg, g, be = self.config, self.ep_group, self.backend
+        ep, epr, k, S = g.ep_size, self.experts_per_rank, cfg.top_k, cfg.num_shared
+        dev = x.device
+
+        ids, w, counts, offsets, sidx, pos = be.route(x, self.gate_weight, self.gate_bias)
+        rows = be.gather(x, sidx)                                    # [T*k, d], destination-rank order
+
+        send_counts = counts.view(ep, epr).contiguous()
+        recv_counts = torch.empty_like(send_counts)
+        g.all_to_all(recv_counts, send_counts)                       # recv[s, e]: rows from s for expert e
+        both = torch.cat([send_counts.flatten(), recv_counts.flatten()]).cpu()
+        send_splits = both[: ep * epr].view(ep, epr).sum(1).tolist()
+        recv_h = both[ep * epr:].view(ep, epr)
+        recv_splits = recv_h.sum(1).tolist()
+        R = int(sum(recv_splits))
+
+        recv = torch.empty(R + S * T, d, dtype=x.dtype, device=dev)
+        g.all_to_all(recv[:R], rows, recv_splits, send_splits)
+        for s in range(S):                                           # shared experts: local tokens
+            recv[R + s * T: R + (s + 1) * T].copy_(x)
+
+        seg_counts = recv_h.flatten().tolist() + [T] * S
+        offs = [0]
+        for c in seg_counts:
+            offs.append(offs[-1] + int(c))
+        seg_offsets = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
+        max_rows = max(seg_counts) if seg_counts else 0
+        out = be.experts(recv, seg_offsets, self._segments(dev), len(seg_counts), max_rows)
+
+        ret = torch.empty(T * k, d, dtype=x.dtype, device=dev)
+        g.all_to_all(ret, out[:R].contiguous(), send_splits, recv_splits)
+        extra = out[R:] if S else None
+        y = be.combine(ret, pos, w, T, extra, S)
+        return y.view(hidden_states.shape)
+
+
+def slice_experts(ex: W4A16Experts, e0: int, e1: int) -> W4A16Experts:
+    """Routed experts [e0, e1) plus every shared expert, from full prepacked weights.
+
+    The prepacked layouts are expert-major, so an expert range is one contiguous slice.
+    """
+    Et = ex.num_experts + ex.num_shared
+
+    def part(t, idx):
+        per = t.numel() // Et
+        return torch.cat([t[i * per:(i + 1) * per] for i in idx]) if idx else t[:0]
+
+    idx = list(range(e0, e1)) + list(range(ex.num_experts, Et))
+    return W4A16Experts(part(ex.w13_packed, idx), part(ex.w13_scales, idx), part(ex.w2_packed, idx),
+                        part(ex.w2_scales, idx), e1 - e0, ex.num_shared, ex.hidden_size, ex.ffn_size,
+                        ex.group_size, None)
+
+
+def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):
+    """Rendezvous from the torchrun environment (comm_group.py:104-138 of the reference)."""
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1 and not dist.is_initialized():
+        kw = dict(backend=backend, timeout=timedelta(seconds=timeout_s))
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(**kw)
+    return ws, rank

@@ -48,7 +48,8 @@ def fused_gate_topk_permute(hidden_states, gate_weight, top_k):
 
 
 def fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias=None, return_logits=False):
-    """[ids int32, weights fp32, counts int32, offsets int32, sorted_idx int32(, logits fp32)]."""
+    """[ids int32, weights fp32, counts int32, offsets int32, sorted_idx int32, positions int32
+    (, logits fp32)] -- positions is the inverse permutation of sorted_idx."""
     return extension().fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias, return_logits)
 
 
@@ -68,10 +69,17 @@ def prepack_w4(qweight, scales, group_size, qweight_up=None, scales_up=None):
 
 
 def w4a16_grouped_gemm(input, packed, packed_scales, expert_offsets, num_experts, N, group_size,
-                       epilogue=0, dest_rows=None, row_scale=None, out_rows=0, max_rows_per_expert=0):
+                       epilogue=0, dest_rows=None, row_scale=None, out_rows=0, max_rows_per_expert=0,
+                       segment_expert=None):
+    """Grouped W4A16 GEMM over `num_experts` row segments (segment_expert maps segment -> weights)."""
     return extension().w4a16_grouped_gemm(input, packed, packed_scales, expert_offsets, num_experts, N,
                                           group_size, epilogue, dest_rows, row_scale, out_rows,
-                                          max_rows_per_expert)
+                                          max_rows_per_expert, segment_expert)
+
+
+def combine_rows(rows, positions, weights, num_tokens, top_k, extra_rows=None, num_extra=0):
+    """y[t] = sum_j weights[t,j] * rows[positions[t,j]] + sum_s extra_rows[s*T + t]."""
+    return extension().combine_rows(rows, positions, weights, num_tokens, top_k, extra_rows, num_extra)
 
 
 def moe_layer_w4a16(x, gate_weight, w13_packed, w13_scales, w2_packed, w2_scales, top_k, ffn_size,

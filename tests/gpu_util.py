@@ -17,7 +17,7 @@ def read_error(ws: torch.Tensor) -> int:
     return int(out[0])
 
 
-def router(x, w, k, bias=None, perm=True, logits=True):
+def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
     """lmoe_fused_gate_topk through the C ABI; returns numpy arrays."""
     T, d = x.shape
     E = w.shape[0]
@@ -29,10 +29,12 @@ def router(x, w, k, bias=None, perm=True, logits=True):
     offsets = torch.empty(E + 1, dtype=torch.int32, device=dev) if perm else None
     sidx = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if perm else None
     lg = torch.empty(T, E, dtype=torch.float32, device=dev) if logits else None
+    pos = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if positions else None
     nbytes = capi.lib().lmoe_router_workspace_bytes(T, E)
     ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
     capi.call("lmoe_fused_gate_topk", x.data_ptr(), w.data_ptr(), capi.ptr(bias), T, d, E, k, ids.data_ptr(),
-              wts.data_ptr(), wbf.data_ptr(), capi.ptr(counts), capi.ptr(offsets), capi.ptr(sidx), capi.ptr(lg),
+              wts.data_ptr(), wbf.data_ptr(), capi.ptr(counts), capi.ptr(offsets), capi.ptr(sidx), capi.ptr(pos),
+              capi.ptr(lg),
               ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     err = read_error(ws)
@@ -42,6 +44,8 @@ def router(x, w, k, bias=None, perm=True, logits=True):
         out.update(counts=counts.cpu().numpy(), offsets=offsets.cpu().numpy(), sorted_idx=sidx[: T * k].cpu().numpy())
     if logits:
         out["logits"] = lg.cpu().numpy()
+    if positions:
+        out["positions"] = pos[: T * k].cpu().numpy()
     return out
 
 
@@ -79,7 +83,7 @@ def prepack(q, s, group_size, q_up=None, s_up=None):
 
 
 def w4_gemm(x, packed, pscale, N, group_size, offsets, epilogue=0, dest=None, row_scale=None, out_rows=None,
-            hint=0):
+            hint=0, seg_expert=None):
     R, K = x.shape
     E = offsets.numel() - 1
     ncols = N // 2 if epilogue == 1 else N
@@ -87,7 +91,8 @@ def w4_gemm(x, packed, pscale, N, group_size, offsets, epilogue=0, dest=None, ro
     out = torch.zeros(rows_out, ncols, dtype=torch.bfloat16, device=x.device)
     ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
     capi.call("lmoe_w4a16_grouped_gemm", x.data_ptr(), R, K, packed.data_ptr(), pscale.data_ptr(), N, group_size,
-              offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, epilogue, capi.ptr(dest),
+              offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, capi.ptr(seg_expert), epilogue,
+              capi.ptr(dest),
               capi.ptr(row_scale), hint, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     assert read_error(ws) == 0

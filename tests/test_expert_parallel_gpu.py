@@ -1,0 +1,96 @@
+"""Expert-parallel layer on GPUs (NCCL): each rank's output must match the single-GPU layer
+on the same tokens with the full expert set (max relative error 1e-2, the layer bar).
+Runs with world size 1 on any box, and with world size 2 when two GPUs are visible."""
+import os
+import socket
+import sys
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, q):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
+        from light_moe_b200.layer import W4A16Experts, W4A16MoELayer
+        E, S, k, d, F, g = case["E"], case["S"], case["k"], case["d"], case["F"], case["g"]
+        gen = torch.Generator(device="cpu").manual_seed(0)
+        gw = (torch.randn(E, d, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        w1 = (torch.randn(E + S, F, d, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        w3 = (torch.randn(E + S, F, d, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        w2 = (torch.randn(E + S, d, F, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        shared = [(w1[E + s], w3[E + s], w2[E + s]) for s in range(S)] or None
+        ex = W4A16Experts.from_dense(w1[:E], w3[:E], w2[:E], g, shared=shared)
+        bias = torch.linspace(-1, 1, E, device=dev) if case.get("bias") else None
+        ep_layer = ExpertParallelW4A16Layer.from_full(gw, ex, k, gate_bias=bias)
+        ref_layer = W4A16MoELayer(gw, ex, k, gate_bias=bias)
+        T = case["T"][rank]
+        x = torch.randn(T, d, generator=torch.Generator(device="cpu").manual_seed(10 + rank)).to(torch.bfloat16).to(dev)
+        for _ in range(2):   # twice: cached segment map, reused buffers
+            y = ep_layer(x)
+        y_ref = ref_layer(x)
+        torch.cuda.synchronize()
+        err = ((y.float() - y_ref.float()).abs().max() / y_ref.float().abs().max()).item()
+        q.put((rank, "ok", err))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+def _run(world, case, timeout=300):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    res = {}
+    while not q.empty():
+        r, st, v = q.get()
+        res[r] = (st, v)
+    return res
+
+
+CASES = [dict(E=8, S=0, k=2, d=512, F=256, g=128, T=[300, 77]),
+         dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[64, 200], bias=True),
+         dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64])]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_ep_world1(case):
+    res = _run(1, case)
+    assert res.get(0, ("missing", None))[0] == "ok", res
+    assert res[0][1] <= 1e-2
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("case", CASES)
+def test_ep_world2(case):
+    res = _run(2, case)
+    for r in range(2):
+        assert res.get(r, ("missing", None))[0] == "ok", res
+        assert res[r][1] <= 1e-2, res
