@@ -157,13 +157,12 @@ def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
     R = T * TOPK
 
     def run():
-        return ops.w4a16_grouped_gemm(xp, ex.w13_packed, ex.w13_scales, offsets, E, 2 * FFN, GROUP, 1, None,
-                                      None, 0, T)
+        return ops.w4a16_grouped_gemm(xp, ex.w13_packed, offsets, E, 2 * FFN, GROUP, 1, None, None, 0, T)
 
     launches = 20
     secs = time_device(run, launches, 3, stream) / launches
     flops = 2.0 * R * (2 * FFN) * D
-    bytes_ = ex.w13_packed.numel() + ex.w13_scales.numel() * 2 + R * D * 2 + R * FFN * 2
+    bytes_ = ex.w13_packed.numel() + R * D * 2 + R * FFN * 2
     if T >= 1024:
         achieved = flops / secs / 1e12
         peak = peaks["bf16_tflops"]
@@ -284,8 +283,7 @@ def run_ours(args):
         if dsecs is not None:
             dsteps = max(args.steps, 20)
             droof = gemm_roofline(xd, gw, ex, T_DECODE, stream, peaks, peak_kind)
-            wbytes = (ex.w13_packed.numel() + ex.w13_scales.numel() * 2 + ex.w2_packed.numel()
-                      + ex.w2_scales.numel() * 2)
+            wbytes = ex.w13_packed.numel() + ex.w2_packed.numel()
             layer_gbs = wbytes / (dsecs / dsteps) / 1e9
             decode = {"tokens": T_DECODE, "value": round(T_DECODE * dsteps / dsecs, 1), "unit": "tokens/s",
                       "ms_per_step": round(dsecs / dsteps * 1e3, 4),

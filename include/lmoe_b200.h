@@ -104,19 +104,20 @@ int lmoe_quantize_w4(const void* w, int w_is_fp32, int64_t rows, int K, int grou
 int lmoe_dequantize_w4(const uint8_t* qweight, const uint16_t* scales, int64_t rows, int K,
                        int group_size, void* out, lmoe_stream_t stream);
 
-/* Sizes of the device ("prepacked") layout streamed by the W4A16 GEMM for `num_experts`
- * matrices of [rows, K]; paired != 0 interleaves two such matrices (gate w1 and up w3) by
- * 64-row blocks, giving 2*rows rows.  K % 64 == 0, group_size % 64 == 0, rows % 128 == 0
- * (rows % 64 == 0 when paired). */
-int lmoe_w4_prepacked_sizes(int num_experts, int rows, int K, int group_size, int paired,
-                            size_t* packed_bytes, size_t* scale_bytes);
+/* Bytes of the device ("prepacked") layout streamed by the W4A16 GEMM for `num_experts`
+ * matrices of [rows, K]: super-blocks of 128 rows x 128 K values with their fp16 scales
+ * embedded, expert-major.  paired != 0 interleaves two such matrices (gate w1 and up w3) by
+ * 64-row blocks, giving 2*rows rows.  K % 128 == 0; group_size a multiple of 64 that
+ * divides 128 or is a multiple of it; rows % 128 == 0 (rows % 64 == 0 when paired). */
+int lmoe_w4_prepacked_bytes(int num_experts, int rows, int K, int group_size, int paired,
+                            size_t* packed_bytes);
 
-/* Canonical int4 weights [num_experts, rows, K/2] (+ scales) -> prepacked layout.  Pass the
+/* Canonical int4 weights [num_experts, rows, K/2] + scales -> prepacked layout.  Pass the
  * up-projection as qweight_b / scales_b to build the paired gate/up layout, else NULL. */
 int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_a,
                     const uint8_t* qweight_b, const uint16_t* scales_b,
                     int num_experts, int rows, int K, int group_size,
-                    uint8_t* packed, uint16_t* packed_scales, lmoe_stream_t stream);
+                    uint8_t* packed, lmoe_stream_t stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* Grouped GEMMs.  Rows [offsets[e], offsets[e+1]) of `input` (bf16 [total_rows, K]) are  */
@@ -135,7 +136,8 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
                            int zero_fill, void* output, void* workspace, size_t workspace_bytes,
                            lmoe_stream_t stream);
 
-/* W4A16: prepacked int4 weights (N rows per expert, N % 128 == 0), fp32 accumulation.
+/* W4A16: prepacked int4 weights (N rows per expert, N % 128 == 0, K % 128 == 0), fp32
+ * accumulation.
  * epilogue 0: output[r, n] = acc                               (ldo >= N)
  * epilogue 1: SwiGLU over a paired gate/up matrix of N = 2*F rows:
  *             output[r, f] = silu(gate[r, f]) * up[r, f]         (ldo >= F)
@@ -147,7 +149,7 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
  * New op; the reference has no W4A16 GEMM (SparseMoEBlockFast's GroupedLinear calls,
  * python/light_moe/model/moe_block.py:249-256, are its dense counterpart). */
 int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
-                            const uint16_t* packed_scales, int N, int group_size,
+                            int N, int group_size,
                             const void* expert_offsets, int offsets_are_int64, int num_experts,
                             const int32_t* segment_expert,
                             int epilogue, const int32_t* dest_rows, const float* row_scale,
@@ -176,7 +178,7 @@ size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int f
                                       int num_experts, int top_k, int num_shared);
 
 /*
- * x        bf16 [num_tokens, hidden_size]    (hidden_size % 128 == 0)
+ * x        bf16 [num_tokens, hidden_size]    (hidden_size % 128 == 0, ffn_size % 128 == 0)
  * gate_*   router weight bf16 [num_experts, hidden_size], optional fp32 bias
  * w13      paired prepacked gate/up weights of num_experts + num_shared experts
  *          (routed experts first), each 2*ffn_size x hidden_size
@@ -188,8 +190,7 @@ size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int f
 int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidden_size,
                          const void* gate_weight, const float* gate_bias, int num_experts,
                          int top_k, int num_shared,
-                         const uint8_t* w13_packed, const uint16_t* w13_scales,
-                         const uint8_t* w2_packed, const uint16_t* w2_scales,
+                         const uint8_t* w13_packed, const uint8_t* w2_packed,
                          int ffn_size, int group_size, void* y,
                          int32_t* ids_out, float* weights_out,
                          void* workspace, size_t workspace_bytes, lmoe_stream_t stream);

@@ -34,16 +34,15 @@ SIGNATURES = {
     "lmoe_permute_rows": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "lmoe_quantize_w4": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P]),
     "lmoe_dequantize_w4": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
-    "lmoe_w4_prepacked_sizes": (_I, [_I, _I, _I, _I, _I, _P, _P]),
-    "lmoe_prepack_w4": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "lmoe_w4_prepacked_bytes": (_I, [_I, _I, _I, _I, _I, _P]),
+    "lmoe_prepack_w4": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "lmoe_gemm_workspace_bytes": (_SZ, []),
     "lmoe_grouped_gemm_bf16": (_I, [_P, _I64, _I, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
-    "lmoe_w4a16_grouped_gemm": (_I, [_P, _I64, _I, _P, _P, _I, _I, _P, _I, _I, _P, _I, _P, _P, _I64, _P, _I64,
-                                     _P, _SZ, _P]),
+    "lmoe_w4a16_grouped_gemm": (_I, [_P, _I64, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _P, _I64, _P, _I64, _P,
+                                     _SZ, _P]),
     "lmoe_combine_rows": (_I, [_P, _P, _P, _I64, _I, _I, _P, _I, _P, _P]),
     "lmoe_moe_layer_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I]),
-    "lmoe_moe_layer_w4a16": (_I, [_P, _I64, _I, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _SZ,
-                                  _P]),
+    "lmoe_moe_layer_w4a16": (_I, [_P, _I64, _I, _P, _P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _P, _P, _SZ, _P]),
 }
 
 _lib = None

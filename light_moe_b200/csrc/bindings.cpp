@@ -179,9 +179,8 @@ torch::Tensor dequantize_w4(torch::Tensor qweight, torch::Tensor scales, int64_t
   return out;
 }
 
-std::tuple<torch::Tensor, torch::Tensor> prepack_w4(torch::Tensor qweight, torch::Tensor scales, int64_t group_size,
-                                                    std::optional<torch::Tensor> qweight_up,
-                                                    std::optional<torch::Tensor> scales_up) {
+torch::Tensor prepack_w4(torch::Tensor qweight, torch::Tensor scales, int64_t group_size,
+                         std::optional<torch::Tensor> qweight_up, std::optional<torch::Tensor> scales_up) {
   check_cuda(qweight, "qweight");
   TORCH_CHECK(qweight.dim() == 3, "qweight must be [E, N, K/2]");
   const c10::cuda::OptionalCUDAGuard guard(qweight.device());
@@ -195,22 +194,18 @@ std::tuple<torch::Tensor, torch::Tensor> prepack_w4(torch::Tensor qweight, torch
     TORCH_CHECK(qb.sizes() == q.sizes() && sb.sizes() == s.sizes(), "gate and up shapes differ");
   }
   const int64_t E = q.size(0), N = q.size(1), K = q.size(2) * 2;
-  size_t pb = 0, sbytes = 0;
-  check_status(lmoe_w4_prepacked_sizes((int)E, (int)N, (int)K, (int)group_size, paired ? 1 : 0, &pb, &sbytes),
-               "prepack_w4");
+  size_t pb = 0;
+  check_status(lmoe_w4_prepacked_bytes((int)E, (int)N, (int)K, (int)group_size, paired ? 1 : 0, &pb), "prepack_w4");
   auto packed = torch::empty({(int64_t)pb}, q.options());
-  auto pscales = torch::empty({(int64_t)(sbytes / 2)}, s.options());
   int st = lmoe_prepack_w4(q.data_ptr<uint8_t>(), reinterpret_cast<const uint16_t*>(s.data_ptr()),
                            paired ? qb.data_ptr<uint8_t>() : nullptr,
                            paired ? reinterpret_cast<const uint16_t*>(sb.data_ptr()) : nullptr, (int)E, (int)N,
-                           (int)K, (int)group_size, packed.data_ptr<uint8_t>(),
-                           reinterpret_cast<uint16_t*>(pscales.data_ptr()), cur_stream());
+                           (int)K, (int)group_size, packed.data_ptr<uint8_t>(), cur_stream());
   check_status(st, "prepack_w4");
-  return {packed, pscales};
+  return packed;
 }
 
-torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torch::Tensor packed_scales,
-                                 torch::Tensor expert_offsets, int64_t num_experts, int64_t N, int64_t group_size,
+torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torch::Tensor expert_offsets, int64_t num_experts, int64_t N, int64_t group_size,
                                  int64_t epilogue, std::optional<torch::Tensor> dest_rows,
                                  std::optional<torch::Tensor> row_scale, int64_t out_rows,
                                  int64_t max_rows_per_expert, std::optional<torch::Tensor> segment_expert) {
@@ -230,8 +225,7 @@ torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torc
   if (segment_expert.has_value() && segment_expert->defined()) se = segment_expert->to(torch::kInt32).contiguous();
   auto ws = workspace((int64_t)lmoe_gemm_workspace_bytes(), x);
   int st = lmoe_w4a16_grouped_gemm(
-      x.data_ptr(), T, (int)K, packed.data_ptr<uint8_t>(), reinterpret_cast<const uint16_t*>(packed_scales.data_ptr()),
-      (int)N, (int)group_size, off.data_ptr(), off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts,
+      x.data_ptr(), T, (int)K, packed.data_ptr<uint8_t>(), (int)N, (int)group_size, off.data_ptr(), off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts,
       se.defined() ? se.data_ptr<int32_t>() : nullptr, (int)epilogue, dr.defined() ? dr.data_ptr<int32_t>() : nullptr, rs.defined() ? rs.data_ptr<float>() : nullptr,
       max_rows_per_expert, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), cur_stream());
   check_status(st, "w4a16_grouped_gemm");
@@ -257,8 +251,7 @@ torch::Tensor combine_rows(torch::Tensor rows, torch::Tensor positions, torch::T
 }
 
 std::vector<torch::Tensor> moe_layer_w4a16(torch::Tensor x, torch::Tensor gate_weight, torch::Tensor w13_packed,
-                                           torch::Tensor w13_scales, torch::Tensor w2_packed,
-                                           torch::Tensor w2_scales, int64_t top_k, int64_t ffn_size,
+                                           torch::Tensor w2_packed, int64_t top_k, int64_t ffn_size,
                                            int64_t group_size, int64_t num_shared,
                                            std::optional<torch::Tensor> gate_bias) {
   check_cuda(x, "x");
@@ -276,9 +269,7 @@ std::vector<torch::Tensor> moe_layer_w4a16(torch::Tensor x, torch::Tensor gate_w
                       xb);
   int st = lmoe_moe_layer_w4a16(xb.data_ptr(), T, (int)d, gw.data_ptr(), b.defined() ? b.data_ptr<float>() : nullptr,
                                 (int)E, (int)top_k, (int)num_shared, w13_packed.data_ptr<uint8_t>(),
-                                reinterpret_cast<const uint16_t*>(w13_scales.data_ptr()),
-                                w2_packed.data_ptr<uint8_t>(), reinterpret_cast<const uint16_t*>(w2_scales.data_ptr()),
-                                (int)ffn_size, (int)group_size, y.data_ptr(), ids.data_ptr<int32_t>(),
+                                w2_packed.data_ptr<uint8_t>(), (int)ffn_size, (int)group_size, y.data_ptr(), ids.data_ptr<int32_t>(),
                                 wts.data_ptr<float>(), ws.data_ptr(), ws.numel(), cur_stream());
   check_status(st, "moe_layer_w4a16");
   return {y, ids, wts};
@@ -304,7 +295,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prepack_w4", &prepack_w4, "Canonical int4 -> GEMM device layout", py::arg("qweight"), py::arg("scales"),
         py::arg("group_size"), py::arg("qweight_up") = py::none(), py::arg("scales_up") = py::none());
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm, "W4A16 grouped GEMM", py::arg("input"), py::arg("packed"),
-        py::arg("packed_scales"), py::arg("expert_offsets"), py::arg("num_experts"), py::arg("N"),
+        py::arg("expert_offsets"), py::arg("num_experts"), py::arg("N"),
         py::arg("group_size"), py::arg("epilogue") = 0, py::arg("dest_rows") = py::none(),
         py::arg("row_scale") = py::none(), py::arg("out_rows") = 0, py::arg("max_rows_per_expert") = 0,
         py::arg("segment_expert") = py::none());
@@ -312,6 +303,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("positions"), py::arg("weights"), py::arg("num_tokens"), py::arg("top_k"),
         py::arg("extra_rows") = py::none(), py::arg("num_extra") = 0);
   m.def("moe_layer_w4a16", &moe_layer_w4a16, "W4A16 MoE layer", py::arg("x"), py::arg("gate_weight"),
-        py::arg("w13_packed"), py::arg("w13_scales"), py::arg("w2_packed"), py::arg("w2_scales"), py::arg("top_k"),
+        py::arg("w13_packed"), py::arg("w2_packed"), py::arg("top_k"),
         py::arg("ffn_size"), py::arg("group_size"), py::arg("num_shared") = 0, py::arg("gate_bias") = py::none());
 }

@@ -1,32 +1,38 @@
 // grouped_gemm.cu -- persistent grouped GEMMs for MoE experts on B200 (sm_100a).
 //
-// For every expert e, rows [offsets[e], offsets[e+1]) of an activation matrix X (bf16,
-// row-major [R, K]) are multiplied by that expert's weight matrix W_e ([N, K]):
-//     Y[r, n] = sum_k X[r, k] * W_e[n, k]
+// For every row segment e (one expert's rows), rows [offsets[e], offsets[e+1]) of an
+// activation matrix X (bf16, row-major [R, K]) are multiplied by that segment's weight
+// matrix W ([N, K]):   Y[r, n] = sum_k X[r, k] * W[n, k]
 // Reference: csrc/grouped_gemm.cu:11-43 (one cuBLAS mm_out per expert after copying the
 // offsets to the host) and python/light_moe/ops/grouped_gemm.py:21-106.  Here one launch
 // covers all experts, the offsets are read on the device, and the weights may be int4.
 //
-// "Swap-AB" formulation: the MMA's M dimension (128) runs over weight rows, N over tokens,
-// so decode-sized batches (a handful of tokens per expert) still fill the 128-row MMA, and
-// the accumulator tile is [128 weight rows x BN tokens] in tensor memory.
+// "Swap-AB": the MMA's M dimension (128) runs over weight rows and N over tokens, so a
+// decode-sized batch (a handful of tokens per expert) still fills the 128-row MMA; the
+// accumulator tile is [128 weight rows x BN tokens] in tensor memory.
 //
-// W4A16 weights (the north-star path): packed int4 blocks (w4_layout.cuh) are bulk-copied
-// into shared memory, dequantised by dedicated warps into bf16 and written with tcgen05.st
-// straight into tensor memory, where tcgen05.mma reads them as the A operand ("TS" form);
-// the token tile (B operand) arrives by TMA with the 128-byte swizzle.  Dequantised value =
-// bf16_rn(q * s), computed exactly as q*s_hi + q*s_lo with one final rounding (s_hi/s_lo
-// split the fp16 scale into two bf16 parts), bit-identical to the CPU oracle.
+// W4A16 weights (the north-star path): one prepacked int4 super-block (128 rows x 128 K,
+// scales embedded, w4_layout.cuh) per pipeline stage arrives by one bulk copy; dequantiser
+// warps turn it into bf16 and write it with tcgen05.st straight into tensor memory, where
+// tcgen05.mma reads it as the A operand ("TS" form); the token tile (B operand) arrives by
+// TMA with the 128-byte swizzle.  Dequantised value = bf16_rn(q * s), computed exactly as
+// q*s_hi + q*s_lo with one final rounding (s_hi / s_lo split the fp16 scale into two bf16
+// parts), bit-identical to the CPU oracle.
 // bf16 weights (the reference's dense grouped_gemm op): the weight tile arrives by TMA too
 // and both operands are read from shared memory ("SS" form).
 //
 // Warp roles (one CTA per SM, persistent over a static round-robin tile schedule):
-//   warp 0            producer: weight blocks (bulk copy or TMA) and token tiles (TMA)
+//   warp 0            token-tile producer (TMA)
 //   warp 1            MMA issuer (one thread)
-//   warps 2..2+DQ-1   int4 dequantisers (W4 only): one weight row per thread
+//   warp 2            weight producer (bulk copy of int4 super-blocks / TMA of bf16 tiles)
+//   warps 3..3+DQ-1   int4 dequantisers (W4 only), DQ/4 groups of 4 warps; a group owns
+//                     every (DQ/4)-th stage, one weight row per thread
 //   last 4 warps      epilogue: TMEM -> registers -> (SwiGLU | scale+scatter) -> global
+// Every stage covers 128 K values (two 64-wide swizzle atoms), so each mbarrier wait,
+// expect-tx and commit is amortised over eight 128 x N x 16 MMAs, and the two producers
+// issue their copies in parallel.
 //
-// Tile order: expert-major, then feature block, then token block (fastest), so the CTAs
+// Tile order: segment-major, then feature block, then token block (fastest), so the CTAs
 // working at the same time share each weight block through L2.
 //
 // Epilogue modes:
@@ -44,20 +50,18 @@ namespace lmoe {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;
+constexpr int kBK = 64;     // one 128-byte swizzle atom of bf16
+constexpr int kSK = 128;    // K values per pipeline stage
 constexpr uint32_t kSite = 0x200u;
 
 struct GemmArgs {
-  // weights
-  const uint8_t* wq;        // W4: prepacked blocks
-  const uint16_t* wscale;   // W4: prepacked scales
-  int group_size;           // W4
-  int G;                    // W4: K / group_size
-  // problem
-  const void* offsets;      // [E+1] row ranges of the segments
+  const uint8_t* wq;          // W4: prepacked super-blocks
+  int group_size;             // W4
+  uint32_t sb_bytes;          // W4: bytes per super-block
+  const void* offsets;        // [E+1] row ranges of the segments
   int offsets_i64;
-  const int32_t* seg_expert; // weight matrix used by each segment (NULL: segment e uses expert e)
-  int E, N, K, NB, KB;      // NB = ceil(N / 128) weight-row blocks, KB = K / 64
+  const int32_t* seg_expert;  // weight matrix of each segment (NULL: segment e uses matrix e)
+  int E, N, K, NB, KS;        // NB = ceil(N / 128) weight-row blocks, KS = K / 128 stages per tile
   int mode;
   __nv_bfloat16* out;
   int64_t ldo;
@@ -67,25 +71,32 @@ struct GemmArgs {
   uint32_t tmem_cols;
 };
 
-template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4>
+template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4, int BOX>
 struct Cfg {
   static constexpr int kDQWarps = W4 ? DQ : 0;
-  static constexpr int kEpiWarp0 = 2 + kDQWarps;
+  static constexpr int kGroups = W4 ? DQ / 4 : 1;
+  static constexpr int kEpiWarp0 = 3 + kDQWarps;
   static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
-  static constexpr uint32_t kBStageBytes = BN * kBK * 2;
-  static constexpr uint32_t kAStageBytes = W4 ? 0u : (uint32_t)(kBM * kBK * 2);   // bf16 weights in smem
-  static constexpr uint32_t kWStageBytes = W4 ? (uint32_t)(kW4BlockBytes + kBM * 2) : 0u;
-  static constexpr int kWStages = W4 ? WST : BST;   // bf16: weight tile travels with the token tile
+  static constexpr uint32_t kBStageBytes = 2u * BN * kBK * 2;                        // [2][BN][64] bf16
+  static constexpr uint32_t kWStageBytes = W4 ? (uint32_t)(kW4SuperInt4Bytes + 512)  // int4 + <= 2 scale groups
+                                              : (uint32_t)(2 * kBM * kBK * 2);       // bf16 [2][128][64]
   static constexpr uint32_t kXchgBytes = 64 * 17 * 4;
-  static constexpr uint32_t kSmemBytes = 1024 + BST * (kBStageBytes + kAStageBytes) + (W4 ? WST * kWStageBytes : 0) +
-                                         kXchgBytes + 1024;
-  static constexpr uint32_t kTmemColsNeeded = ACC * BN + (W4 ? AST * 32 : 0);
+  static constexpr uint32_t kSmemBytes = 1024 + BST * kBStageBytes + WST * kWStageBytes + kXchgBytes + 1024;
+  static constexpr uint32_t kTmemColsNeeded = ACC * BN + (W4 ? AST * 64 : 0);
+  // dequantise a whole stage into registers before waiting for its TMEM stage when the
+  // register file allows it (65536 registers / threads >= ~128)
+  static constexpr bool kEarlyDequant = kThreads <= 512;
+  static_assert(BN % BOX == 0 && BOX % 8 == 0 && BN % 16 == 0, "token tile = whole boxes of whole swizzle atoms");
+  static_assert(!W4 || DQ % 4 == 0, "dequantiser groups of four warps");
+  // A stage ring may only be waited on by one group: an mbarrier parity wait is exact only
+  // while the waiter is at most one phase ahead, so every stage must have a single owner.
+  static_assert(!W4 || (WST % kGroups == 0 && AST % kGroups == 0), "stages per dequantiser group");
 };
 
 struct __align__(8) GemmBars {
   uint64_t w_full[16], w_empty[16];
-  uint64_t b_full[8], b_empty[8];
-  uint64_t a_full[16], a_empty[16];
+  uint64_t b_full[16], b_empty[16];
+  uint64_t a_full[8], a_empty[8];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -100,9 +111,9 @@ struct TileInfo {
   int e, w, fb, row0, rows;   // segment, its weight matrix, feature block, first row, rows
 };
 
-// Tiles are numbered expert-major, then feature block, then token block (fastest).
+// Tiles are numbered segment-major, then feature block, then token block (fastest).
 template <int BN>
-__device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_hint, int NB) {
+__device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_hint) {
   int e = e_hint;
   while (tile >= b->tile_start[e + 1]) ++e;
   e_hint = e;
@@ -135,19 +146,27 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __nv_bfloat162 s_hi, __
   }
 }
 
+// Exact split of an fp16 scale into bf16 hi (top 8 significant bits) + lo (the rest).
+__device__ __forceinline__ void split_scale(uint16_t sbits, __nv_bfloat162& s_hi, __nv_bfloat162& s_lo) {
+  const float sf = __half2float(__ushort_as_half(sbits));
+  const __nv_bfloat16 hi = __float2bfloat16_rz(sf);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(sf, __bfloat162float(hi)));
+  s_hi = __nv_bfloat162(hi, hi);
+  s_lo = __nv_bfloat162(lo, lo);
+}
+
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4>
-__global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads, 1)
+template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4, int BOX>
+__global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const GemmArgs a) {
-  using C = Cfg<BN, DQ, WST, BST, AST, ACC, W4>;
+  using C = Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* b_stages = base;                                           // BST x [BN x 64] bf16 (SW128)
-  uint8_t* a_stages = b_stages + BST * C::kBStageBytes;               // bf16 path: BST x [128 x 64]
-  uint8_t* w_stages = a_stages + BST * C::kAStageBytes;               // W4 path: WST x (4096 + 256)
-  float* xchg = reinterpret_cast<float*>(w_stages + (W4 ? WST * C::kWStageBytes : 0));
+  uint8_t* b_stages = base;                                    // BST x [2][BN][64] bf16 (SW128)
+  uint8_t* w_stages = b_stages + BST * C::kBStageBytes;        // WST x (int4 super-block | bf16 [2][128][64])
+  float* xchg = reinterpret_cast<float*>(w_stages + WST * C::kWStageBytes);
   GemmBars* bars = reinterpret_cast<GemmBars*>(reinterpret_cast<uint8_t*>(xchg) + C::kXchgBytes);
   volatile int* abort_flag = &bars->abort;
 
@@ -156,16 +175,16 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
   const int lane = tid & 31;
 
   if (tid == 0) {
-    for (int s = 0; s < C::kWStages; ++s) {
+    for (int s = 0; s < WST; ++s) {
       mbar_init(&bars->w_full[s], 1);
-      mbar_init(&bars->w_empty[s], W4 ? 4 : 1);
+      mbar_init(&bars->w_empty[s], W4 ? 4 : 1);   // W4: the 4 warps of the owning group
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bars->b_full[s], 1);
       mbar_init(&bars->b_empty[s], 1);
     }
     for (int s = 0; s < AST; ++s) {
-      mbar_init(&bars->a_full[s], W4 ? 4 : 1);
+      mbar_init(&bars->a_full[s], 4);
       mbar_init(&bars->a_empty[s], 1);
     }
     for (int s = 0; s < ACC; ++s) {
@@ -176,15 +195,13 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
     bars->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_x);
-    if (!W4) tma_prefetch_desc(&tm_w);
-  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_x);
+  if (!W4 && warp == 2 && lane == 0) tma_prefetch_desc(&tm_w);
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, a.tmem_cols);
     tmem_relinquish();
   }
-  // expert row offsets and the tile prefix (computed redundantly by every CTA)
+  // segment row offsets, weight map and the tile prefix (computed redundantly by every CTA)
   for (int e = tid; e <= a.E; e += C::kThreads) {
     bars->row_off[e] = a.offsets_i64 ? (int)static_cast<const int64_t*>(a.offsets)[e]
                                      : static_cast<const int32_t*>(a.offsets)[e];
@@ -209,96 +226,104 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_a = tmem + ACC * BN;   // W4: AST stages of 32 columns
+  const uint32_t tmem_a = tmem + ACC * BN;   // W4: AST stages of 64 columns
   const int total = bars->total_tiles;
-  const int KB = a.KB;
+  const int KS = a.KS;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+    // ------------------------------------------------------------------ token-tile producer
     if (lane == 0) {
-      uint32_t wit = 0, bit = 0;
+      uint32_t it = 0;
       int e_hint = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB);
-        const uint8_t* wblk = nullptr;
-        const uint16_t* sblk = nullptr;
-        if (W4) {
-          wblk = a.wq + (size_t)(ti.w * a.NB + ti.fb) * KB * kW4BlockBytes;
-          sblk = a.wscale + (size_t)(ti.w * a.NB + ti.fb) * a.G * kBM;
+        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
+        const int nbox = (ti.rows + BOX - 1) / BOX;   // only the boxes that cover this tile's rows
+        const uint32_t bytes = (uint32_t)(2 * nbox * BOX * kBK * 2);
+        for (int ks = 0; ks < KS; ++ks, ++it) {
+          const int s = it % BST;
+          if (!mbar_wait(&bars->b_empty[s], ((it / BST) & 1u) ^ 1u, a.err, abort_flag, kSite + 1)) { ok = false; break; }
+          uint8_t* bsm = b_stages + s * C::kBStageBytes;
+          mbar_arrive_expect_tx(&bars->b_full[s], bytes);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            for (int bx = 0; bx < nbox; ++bx)
+              tma_load_2d(bsm + (j * BN + bx * BOX) * kBK * 2, &tm_x, &bars->b_full[s], (2 * ks + j) * kBK,
+                          ti.row0 + bx * BOX);
         }
-        for (int kb = 0; kb < KB; ++kb) {
+      }
+      const uint32_t first = it > (uint32_t)BST ? it - BST : 0u;   // drain copies in flight
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->b_full[j % BST], (j / BST) & 1u, a.err, nullptr, kSite + 2);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int e_hint = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
+        const uint8_t* wblk = W4 ? a.wq + (size_t)(ti.w * a.NB + ti.fb) * KS * a.sb_bytes : nullptr;
+        for (int ks = 0; ks < KS; ++ks, ++it) {
+          const int s = it % WST;
+          if (!mbar_wait(&bars->w_empty[s], ((it / WST) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)) { ok = false; break; }
+          uint8_t* wsm = w_stages + s * C::kWStageBytes;
           if (W4) {
-            const int s = wit % WST;
-            if (!mbar_wait(&bars->w_empty[s], ((wit / WST) & 1u) ^ 1u, a.err, abort_flag, kSite + 1)) { ok = false; break; }
-            uint8_t* wsm = w_stages + s * C::kWStageBytes;
-            mbar_arrive_expect_tx(&bars->w_full[s], kW4BlockBytes + kBM * 2);
-            bulk_load(wsm, wblk + (size_t)kb * kW4BlockBytes, kW4BlockBytes, &bars->w_full[s]);
-            bulk_load(wsm + kW4BlockBytes, sblk + (size_t)((kb * kBK) / a.group_size) * kBM, kBM * 2,
-                      &bars->w_full[s]);
-            ++wit;
-          }
-          const int s2 = bit % BST;
-          if (!mbar_wait(&bars->b_empty[s2], ((bit / BST) & 1u) ^ 1u, a.err, abort_flag, kSite + 2)) { ok = false; break; }
-          uint8_t* bsm = b_stages + s2 * C::kBStageBytes;
-          if (W4) {
-            mbar_arrive_expect_tx(&bars->b_full[s2], C::kBStageBytes);
+            mbar_arrive_expect_tx(&bars->w_full[s], a.sb_bytes);
+            bulk_load(wsm, wblk + (size_t)ks * a.sb_bytes, a.sb_bytes, &bars->w_full[s]);
           } else {
-            mbar_arrive_expect_tx(&bars->b_full[s2], C::kBStageBytes + C::kAStageBytes);
-            tma_load_2d(a_stages + s2 * C::kAStageBytes, &tm_w, &bars->b_full[s2], kb * kBK,
-                        ti.w * a.N + ti.fb * kBM);
+            mbar_arrive_expect_tx(&bars->w_full[s], 2 * kBM * kBK * 2);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_2d(wsm + j * kBM * kBK * 2, &tm_w, &bars->w_full[s], (2 * ks + j) * kBK,
+                          ti.w * a.N + ti.fb * kBM);
           }
-          tma_load_2d(bsm, &tm_x, &bars->b_full[s2], kb * kBK, ti.row0);
-          ++bit;
         }
       }
-      // drain: no bulk copy may still be landing when the CTA exits
-      const uint32_t bfirst = bit > (uint32_t)BST ? bit - BST : 0u;
-      for (uint32_t j = bfirst; j < bit; ++j) mbar_wait(&bars->b_full[j % BST], (j / BST) & 1u, a.err, nullptr, kSite + 3);
-      if (W4) {
-        const uint32_t wfirst = wit > (uint32_t)WST ? wit - WST : 0u;
-        for (uint32_t j = wfirst; j < wit; ++j) mbar_wait(&bars->w_full[j % WST], (j / WST) & 1u, a.err, nullptr, kSite + 4);
-      }
+      const uint32_t first = it > (uint32_t)WST ? it - WST : 0u;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->w_full[j % WST], (j / WST) & 1u, a.err, nullptr, kSite + 4);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t ait = 0, bit = 0, lt = 0;
+      uint32_t it = 0, lt = 0;
       int e_hint = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++lt) {
-        const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB);
+        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
         const uint32_t n_eff = (uint32_t)((ti.rows + 15) & ~15);
         const uint32_t idesc = idesc_bf16_f32(kBM, n_eff);
         const uint32_t acc = lt % ACC;
         if (!mbar_wait(&bars->acc_empty[acc], ((lt / ACC) & 1u) ^ 1u, a.err, abort_flag, kSite + 5)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
-        for (int kb = 0; kb < KB; ++kb) {
-          const int s2 = bit % BST;
+        for (int ks = 0; ks < KS; ++ks, ++it) {
+          const int sb = it % BST;
+          const int sa = it % (W4 ? AST : WST);
           if (W4) {
-            const int as = ait % AST;
-            if (!mbar_wait(&bars->a_full[as], (ait / AST) & 1u, a.err, abort_flag, kSite + 6)) { ok = false; break; }
-          }
-          if (!mbar_wait(&bars->b_full[s2], (bit / BST) & 1u, a.err, abort_flag, kSite + 7)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t bsm = smem_u32(b_stages + s2 * C::kBStageBytes);
-          if (W4) {
-            const uint32_t as_col = tmem_a + (ait % AST) * 32;
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_ts(d_tmem, as_col + kk * 8, sdesc_k_sw128(bsm + kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
-            mma_commit(&bars->a_empty[ait % AST]);
-            ++ait;
+            if (!mbar_wait(&bars->a_full[sa], (it / AST) & 1u, a.err, abort_flag, kSite + 6)) { ok = false; break; }
           } else {
-            const uint32_t asm_ = smem_u32(a_stages + s2 * C::kAStageBytes);
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_ss(d_tmem, sdesc_k_sw128(asm_ + kk * 32), sdesc_k_sw128(bsm + kk * 32), idesc,
-                     (kb | kk) != 0 ? 1u : 0u);
+            if (!mbar_wait(&bars->w_full[sa], (it / WST) & 1u, a.err, abort_flag, kSite + 6)) { ok = false; break; }
           }
-          mma_commit(&bars->b_empty[s2]);
-          ++bit;
+          if (!mbar_wait(&bars->b_full[sb], (it / BST) & 1u, a.err, abort_flag, kSite + 7)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t bsm = smem_u32(b_stages + sb * C::kBStageBytes);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t bdesc = sdesc_k_sw128(bsm + j * BN * kBK * 2 + kk * 32);
+              const uint32_t accum = (ks | j | kk) != 0 ? 1u : 0u;
+              if (W4) {
+                mma_ts(d_tmem, tmem_a + sa * 64 + j * 32 + kk * 8, bdesc, idesc, accum);
+              } else {
+                const uint32_t asm_ = smem_u32(w_stages + sa * C::kWStageBytes) + j * kBM * kBK * 2;
+                mma_ss(d_tmem, sdesc_k_sw128(asm_ + kk * 32), bdesc, idesc, accum);
+              }
+            }
+          }
+          mma_commit(W4 ? &bars->a_empty[sa] : &bars->w_empty[sa]);
+          mma_commit(&bars->b_empty[sb]);
         }
         if (ok) mma_commit(&bars->acc_full[acc]);
       }
@@ -307,63 +332,85 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
     }
   } else if (W4 && warp < C::kEpiWarp0) {
     // ------------------------------------------------------------------ int4 dequantisers
-    // DQ / 4 groups of 4 warps (one warp per TMEM lane quarter, one weight row per thread).
-    // Group g owns every (DQ/4)-th k-block, so several k-blocks are dequantised at once and
-    // the barrier / shared-load / tensor-memory-store latency of one block overlaps the
-    // arithmetic of the others.
-    constexpr int kGroups = DQ / 4;
-    const int grp = (warp - 2) >> 2;
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
+    // Group g owns every kGroups-th stage, so several stages are dequantised at once and
+    // the barrier / shared-load / tensor-memory-store latency of one overlaps the others.
+    const int grp = (warp - 3) >> 2;
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;   // weight row within the tile
+    const int sg = w4_scale_groups(a.group_size);
     const __nv_bfloat162 off136 = __floats2bfloat162_rn(136.0f, 136.0f);
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        if ((int)(it % kGroups) != grp) continue;
+      for (int ks = 0; ks < KS; ++ks, ++it) {
+        if ((int)(it % C::kGroups) != grp) continue;
         const int s = it % WST;
         if (!mbar_wait(&bars->w_full[s], (it / WST) & 1u, a.err, abort_flag, kSite + 10)) { ok = false; break; }
         const uint8_t* wsm = w_stages + s * C::kWStageBytes;
-        const uint4 v0 = *reinterpret_cast<const uint4*>(wsm + row * 16);
-        const uint4 v1 = *reinterpret_cast<const uint4*>(wsm + 2048 + row * 16);
-        const uint16_t sbits = reinterpret_cast<const uint16_t*>(wsm + kW4BlockBytes)[row];
+        uint4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4*>(wsm + i * 2048 + row * 16);
+        const uint16_t* scl = reinterpret_cast<const uint16_t*>(wsm + kW4SuperInt4Bytes);
+        const uint16_t sb0 = scl[row];
+        const uint16_t sb1 = scl[(sg > 1 ? 128 : 0) + row];   // second k-block: next group when g == 64
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->w_empty[s]);
-        // exact split of the fp16 scale into bf16 hi + lo parts
-        const float sf = __half2float(__ushort_as_half(sbits));
-        const __nv_bfloat16 shi = __float2bfloat16_rz(sf);
-        const __nv_bfloat16 slo = __float2bfloat16_rn(__fsub_rn(sf, __bfloat162float(shi)));
-        const __nv_bfloat162 s_hi = __nv_bfloat162(shi, shi);
-        const __nv_bfloat162 s_lo = __nv_bfloat162(slo, slo);
-        uint32_t o0[16], o1[16];
-        dequant_word(v0.x, s_hi, s_lo, off136, &o0[0]);
-        dequant_word(v0.y, s_hi, s_lo, off136, &o0[4]);
-        dequant_word(v0.z, s_hi, s_lo, off136, &o0[8]);
-        dequant_word(v0.w, s_hi, s_lo, off136, &o0[12]);
-        dequant_word(v1.x, s_hi, s_lo, off136, &o1[0]);
-        dequant_word(v1.y, s_hi, s_lo, off136, &o1[4]);
-        dequant_word(v1.z, s_hi, s_lo, off136, &o1[8]);
-        dequant_word(v1.w, s_hi, s_lo, off136, &o1[12]);
         const int as = it % AST;
-        if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t taddr = tmem_a + ((uint32_t)(q * 32) << 16) + as * 32;
-        tmem_st16(taddr, o0);
-        tmem_st16(taddr + 16, o1);
+        const uint32_t taddr = tmem_a + ((uint32_t)(q * 32) << 16) + as * 64;
+        if constexpr (C::kEarlyDequant) {
+          // enough registers: dequantise the whole stage first, then wait for the TMEM stage
+          uint32_t o[4][16];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            __nv_bfloat162 s_hi, s_lo;
+            split_scale(j == 0 ? sb0 : sb1, s_hi, s_lo);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint4 w4 = v[2 * j + h];
+              dequant_word(w4.x, s_hi, s_lo, off136, &o[2 * j + h][0]);
+              dequant_word(w4.y, s_hi, s_lo, off136, &o[2 * j + h][4]);
+              dequant_word(w4.z, s_hi, s_lo, off136, &o[2 * j + h][8]);
+              dequant_word(w4.w, s_hi, s_lo, off136, &o[2 * j + h][12]);
+            }
+          }
+          if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_st16(taddr + c * 16, o[c]);
+        } else {
+          // register-limited (many warps): dequantise and store 16 columns at a time
+          if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            __nv_bfloat162 s_hi, s_lo;
+            split_scale(j == 0 ? sb0 : sb1, s_hi, s_lo);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t o[16];
+              const uint4 w4 = v[2 * j + h];
+              dequant_word(w4.x, s_hi, s_lo, off136, &o[0]);
+              dequant_word(w4.y, s_hi, s_lo, off136, &o[4]);
+              dequant_word(w4.z, s_hi, s_lo, off136, &o[8]);
+              dequant_word(w4.w, s_hi, s_lo, off136, &o[12]);
+              tmem_st16(taddr + (2 * j + h) * 16, o);
+            }
+          }
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->a_full[as]);
       }
     }
-  } else {
+  } else if (warp >= C::kEpiWarp0) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = q * 32 + lane;
     uint32_t lt = 0;
     int e_hint = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++lt) {
-      const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB);
+      const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
       const int n_eff = (ti.rows + 15) & ~15;
       const uint32_t acc = lt % ACC;
       if (!mbar_wait(&bars->acc_full[acc], (lt / ACC) & 1u, a.err, abort_flag, kSite + 12)) break;
@@ -421,16 +468,18 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4>::kThreads,
   }
 }
 
-template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4>
+template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4, int BOX>
 int launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, GemmArgs a, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, DQ, WST, BST, AST, ACC, W4>;
+  using C = Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>;
   static_assert(C::kTmemColsNeeded <= 512, "tensor memory budget");
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
+  static_assert(C::kSmemBytes + sizeof(GemmBars) <= 232448, "shared memory budget");
+  static_assert(WST <= 16 && BST <= 16 && AST <= 8 && ACC <= 2, "barrier arrays");
+  static_assert(!W4 || (AST >= 1 && WST >= DQ / 4), "every dequantiser group needs a weight stage");
   uint32_t cols = 32;
   while (cols < C::kTmemColsNeeded) cols <<= 1;
   a.tmem_cols = cols;
   const size_t smem = C::kSmemBytes + sizeof(GemmBars);
-  auto fn = grouped_gemm_kernel<BN, DQ, WST, BST, AST, ACC, W4>;
+  auto fn = grouped_gemm_kernel<BN, DQ, WST, BST, AST, ACC, W4, BOX>;
   LMOE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   fn<<<grid, C::kThreads, smem, stream>>>(tm_x, tm_w, a);
   return cuda_status(cudaGetLastError());
@@ -438,19 +487,20 @@ int launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, GemmArgs a, in
 
 }  // namespace
 
-// Internal entry used by the C-ABI wrappers below and by the layer driver.
+// Internal entry used by the C-ABI wrappers and by the layer driver.
 int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   DeviceInfo dev;
   int st = get_device_info(&dev);
   if (st != LMOE_OK) return st;
   if (dev.cc_major != 10) return LMOE_ERR_DEVICE;
   if (p.num_experts < 1 || p.num_experts > kMaxGemmExperts) return LMOE_ERR_UNSUPPORTED;
-  if (p.K < kBK || p.K % kBK) return LMOE_ERR_INVALID_ARG;
+  if (p.K < kSK || p.K % kSK) return LMOE_ERR_UNSUPPORTED;
   if (p.total_rows < 0 || p.total_rows > INT32_MAX) return LMOE_ERR_INVALID_ARG;
   if (!p.x || !p.offsets || !p.out || !p.err) return LMOE_ERR_INVALID_ARG;
   const bool w4 = p.wq != nullptr;
   if (w4) {
-    if (!p.wscale || p.group_size < kBK || p.group_size % kBK || p.K % p.group_size) return LMOE_ERR_UNSUPPORTED;
+    const int g = p.group_size;
+    if (g < kBK || g % kBK || p.K % g || (g < kSK && kSK % g)) return LMOE_ERR_UNSUPPORTED;
     if (p.N % kBM) return LMOE_ERR_UNSUPPORTED;
   } else {
     if (!p.w) return LMOE_ERR_INVALID_ARG;
@@ -461,9 +511,8 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
 
   GemmArgs a = {};
   a.wq = p.wq;
-  a.wscale = p.wscale;
   a.group_size = p.group_size;
-  a.G = w4 ? p.K / p.group_size : 0;
+  a.sb_bytes = w4 ? (uint32_t)w4_super_bytes(p.group_size) : 0u;
   a.offsets = p.offsets;
   a.offsets_i64 = p.offsets_i64;
   a.seg_expert = p.seg_expert;
@@ -471,7 +520,7 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.N = p.N;
   a.K = p.K;
   a.NB = (p.N + kBM - 1) / kBM;
-  a.KB = p.K / kBK;
+  a.KS = p.K / kSK;
   a.mode = p.mode;
   a.out = static_cast<__nv_bfloat16*>(p.out);
   a.ldo = p.ldo;
@@ -480,10 +529,12 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.err = p.err;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
-  const int BNsel = small ? 64 : 192;
+  // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),
+  // the whole 192-row tile otherwise
+  const int box = small ? 16 : 192;
   CUtensorMap tm_x, tm_w;
   st = encode_tmap_2d(&tm_x, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,
-                      (uint64_t)p.ldx * 2, (uint32_t)BNsel, kBK, true);
+                      (uint64_t)p.ldx * 2, (uint32_t)box, kBK, true);
   if (st != LMOE_OK) return st;
   if (!w4) {
     st = encode_tmap_2d(&tm_w, p.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.num_experts * p.N,
@@ -494,11 +545,12 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   }
   const int grid = dev.num_sms;
   if (w4) {
-    if (small) return launch_gemm<64, 16, 16, 4, 8, 2, true>(tm_x, tm_w, a, grid, stream);
-    return launch_gemm<192, 12, 8, 4, 4, 2, true>(tm_x, tm_w, a, grid, stream);
+    //                          BN  DQ WST BST AST ACC  W4   BOX
+    if (small) return launch_gemm<64, 16, 12, 6, 4, 2, true, 16>(tm_x, tm_w, a, grid, stream);
+    return launch_gemm<192, 8, 6, 3, 2, 2, true, 192>(tm_x, tm_w, a, grid, stream);
   }
-  if (small) return launch_gemm<64, 0, 1, 6, 1, 2, false>(tm_x, tm_w, a, grid, stream);
-  return launch_gemm<192, 0, 1, 4, 1, 2, false>(tm_x, tm_w, a, grid, stream);
+  if (small) return launch_gemm<64, 0, 4, 4, 1, 2, false, 16>(tm_x, tm_w, a, grid, stream);
+  return launch_gemm<192, 0, 2, 3, 1, 2, false, 192>(tm_x, tm_w, a, grid, stream);
 }
 
 }  // namespace lmoe

@@ -27,9 +27,8 @@ struct GemmProblem {
   // weight matrix of each segment (NULL: segment e uses matrix e); lets rows that arrive
   // grouped by (source rank, expert) be multiplied without a local re-sort
   const int32_t* seg_expert = nullptr;
-  // weights: either W4 prepacked (wq + wscale) or bf16 [num_experts, N, K] (w)
+  // weights: either W4 prepacked super-blocks (wq, scales embedded) or bf16 [num_experts, N, K] (w)
   const uint8_t* wq = nullptr;
-  const uint16_t* wscale = nullptr;
   int group_size = 0;
   const void* w = nullptr;
   int N = 0;  // weight rows per expert (for SwiGLU: 2 * features)

@@ -23,58 +23,66 @@ namespace lmoe {
 namespace {
 
 // ------------------------------------------------------------------------------------ prepack
-// One thread per output 16-byte chunk: (e, fb, kb, half, row).
+// Output super-block (e, fb, sb) of w4_layout.cuh.  Source rows: plain blocks of 128 rows,
+// or (paired) 64 rows of A followed by the same 64 rows of B.
+__device__ __forceinline__ int64_t prepack_src_row(int e, int rows_in, int fb, int r, int paired) {
+  return paired ? (int64_t)e * rows_in + fb * 64 + (r & 63) : (int64_t)e * rows_in + fb * kW4BlockRows + r;
+}
+
+// int4 part: one thread per output 16-byte chunk (e, fb, sb, j, h, row).
 __global__ void prepack_w4_kernel(const uint8_t* __restrict__ qa, const uint8_t* __restrict__ qb, int E, int rows_in,
-                                  int K, uint8_t* __restrict__ out, int paired) {
+                                  int K, int sb_bytes, uint8_t* __restrict__ out, int paired) {
   const int NB = paired ? rows_in / 64 : rows_in / kW4BlockRows;
-  const int KB = K / kW4BlockK;
-  const int64_t total = (int64_t)E * NB * KB * 2 * kW4BlockRows;
+  const int KSB = K / kW4SuperK;
+  const int64_t total = (int64_t)E * NB * KSB * 4 * kW4BlockRows;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int r = (int)(i % kW4BlockRows);
   int64_t rest = i / kW4BlockRows;
-  const int h = (int)(rest % 2);
-  rest /= 2;
-  const int kb = (int)(rest % KB);
-  rest /= KB;
+  const int jh = (int)(rest % 4);   // k-block j = jh / 2, half h = jh % 2
+  rest /= 4;
+  const int sb = (int)(rest % KSB);
+  rest /= KSB;
   const int fb = (int)(rest % NB);
   const int e = (int)(rest / NB);
-  const uint8_t* src;
-  int64_t srow;
-  if (paired) {
-    src = r < 64 ? qa : qb;
-    srow = (int64_t)e * rows_in + fb * 64 + (r & 63);
-  } else {
-    src = qa;
-    srow = (int64_t)e * rows_in + fb * kW4BlockRows + r;
-  }
-  const uint4 c = *reinterpret_cast<const uint4*>(src + srow * (K / 2) + (kb * kW4BlockK + h * 32) / 2);
+  const uint8_t* src = (paired && r >= 64) ? qb : qa;
+  const int64_t srow = prepack_src_row(e, rows_in, fb, r, paired);
+  const int k0 = sb * kW4SuperK + (jh >> 1) * 64 + (jh & 1) * 32;
+  const uint4 c = *reinterpret_cast<const uint4*>(src + srow * (K / 2) + k0 / 2);
   uint4 o;
   o.x = w4_interleave_word(c.x);
   o.y = w4_interleave_word(c.y);
   o.z = w4_interleave_word(c.z);
   o.w = w4_interleave_word(c.w);
-  reinterpret_cast<uint4*>(out)[i] = o;
+  uint8_t* dst = out + ((int64_t)(e * NB + fb) * KSB + sb) * sb_bytes + jh * 2048 + r * 16;
+  *reinterpret_cast<uint4*>(dst) = o;
 }
 
-__global__ void prepack_scales_kernel(const uint16_t* __restrict__ sa, const uint16_t* __restrict__ sb, int E,
-                                      int rows_in, int G, uint16_t* __restrict__ out, int paired) {
+// scale part: one thread per (e, fb, sb, group-in-super-block, row).
+__global__ void prepack_scales_kernel(const uint16_t* __restrict__ sa, const uint16_t* __restrict__ sb_in, int E,
+                                      int rows_in, int K, int g, int sb_bytes, uint8_t* __restrict__ out,
+                                      int paired) {
   const int NB = paired ? rows_in / 64 : rows_in / kW4BlockRows;
-  const int64_t total = (int64_t)E * NB * G * kW4BlockRows;
+  const int KSB = K / kW4SuperK;
+  const int SG = w4_scale_groups(g);
+  const int G = K / g;
+  const int64_t total = (int64_t)E * NB * KSB * SG * kW4BlockRows;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int r = (int)(i % kW4BlockRows);
   int64_t rest = i / kW4BlockRows;
-  const int g = (int)(rest % G);
-  rest /= G;
+  const int gi = (int)(rest % SG);
+  rest /= SG;
+  const int sb = (int)(rest % KSB);
+  rest /= KSB;
   const int fb = (int)(rest % NB);
   const int e = (int)(rest / NB);
-  if (paired) {
-    const uint16_t* src = r < 64 ? sa : sb;
-    out[i] = src[((int64_t)e * rows_in + fb * 64 + (r & 63)) * G + g];
-  } else {
-    out[i] = sa[((int64_t)e * rows_in + fb * kW4BlockRows + r) * G + g];
-  }
+  const uint16_t* src = (paired && r >= 64) ? sb_in : sa;
+  const int64_t srow = prepack_src_row(e, rows_in, fb, r, paired);
+  const int group = (sb * kW4SuperK + gi * (g < kW4SuperK ? g : 0)) / g;
+  uint16_t* dst = reinterpret_cast<uint16_t*>(out + ((int64_t)(e * NB + fb) * KSB + sb) * sb_bytes +
+                                              kW4SuperInt4Bytes + gi * 256) + r;
+  *dst = src[srow * G + group];
 }
 
 // ------------------------------------------------------------------------------------ routing table
@@ -198,36 +206,38 @@ using namespace lmoe;
 
 // ---------------------------------------------------------------------------------- C ABI
 
-extern "C" int lmoe_w4_prepacked_sizes(int num_experts, int rows, int K, int group_size, int paired,
-                                       size_t* packed_bytes, size_t* scale_bytes) {
-  LMOE_ARG_CHECK(num_experts >= 1 && rows > 0 && K > 0 && group_size > 0);
-  LMOE_ARG_CHECK(K % kW4BlockK == 0 && K % group_size == 0 && group_size % kW4BlockK == 0);
+extern "C" int lmoe_w4_prepacked_bytes(int num_experts, int rows, int K, int group_size, int paired,
+                                       size_t* packed_bytes) {
+  LMOE_ARG_CHECK(num_experts >= 1 && rows > 0 && K > 0 && group_size > 0 && packed_bytes);
+  LMOE_ARG_CHECK(K % kW4SuperK == 0 && K % group_size == 0 && group_size % 64 == 0);
+  LMOE_ARG_CHECK(group_size >= kW4SuperK || kW4SuperK % group_size == 0);
   LMOE_ARG_CHECK(paired ? rows % 64 == 0 : rows % kW4BlockRows == 0);
   const int64_t out_rows = (int64_t)(paired ? 2 * rows : rows);
-  if (packed_bytes) *packed_bytes = (size_t)num_experts * out_rows * (K / 2);
-  if (scale_bytes) *scale_bytes = (size_t)num_experts * out_rows * (K / group_size) * sizeof(uint16_t);
+  *packed_bytes = (size_t)num_experts * (out_rows / kW4BlockRows) * (K / kW4SuperK) * w4_super_bytes(group_size);
   return LMOE_OK;
 }
 
 extern "C" int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_a, const uint8_t* qweight_b,
                                const uint16_t* scales_b, int num_experts, int rows, int K, int group_size,
-                               uint8_t* packed, uint16_t* packed_scales, lmoe_stream_t stream_) {
+                               uint8_t* packed, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const int paired = qweight_b != nullptr;
-  size_t pb = 0, sb = 0;
-  int st = lmoe_w4_prepacked_sizes(num_experts, rows, K, group_size, paired, &pb, &sb);
+  size_t pb = 0;
+  int st = lmoe_w4_prepacked_bytes(num_experts, rows, K, group_size, paired, &pb);
   if (st != LMOE_OK) return st;
-  LMOE_ARG_CHECK(qweight_a && scales_a && packed && packed_scales);
+  LMOE_ARG_CHECK(qweight_a && scales_a && packed);
   LMOE_ARG_CHECK(!paired || scales_b);
   LMOE_ARG_CHECK(aligned16(qweight_a) && (!paired || aligned16(qweight_b)) && aligned16(packed));
   const int threads = 256;
-  const int64_t chunks = (int64_t)pb / 16;
+  const int NB = paired ? rows / 64 : rows / kW4BlockRows;
+  const int64_t chunks = (int64_t)num_experts * NB * (K / kW4SuperK) * 4 * kW4BlockRows;
+  const int sbb = w4_super_bytes(group_size);
   prepack_w4_kernel<<<(unsigned)((chunks + threads - 1) / threads), threads, 0, stream>>>(
-      qweight_a, qweight_b, num_experts, rows, K, packed, paired);
+      qweight_a, qweight_b, num_experts, rows, K, sbb, packed, paired);
   LMOE_CUDA_TRY(cudaGetLastError());
-  const int64_t ns = (int64_t)sb / 2;
+  const int64_t ns = (int64_t)num_experts * NB * (K / kW4SuperK) * w4_scale_groups(group_size) * kW4BlockRows;
   prepack_scales_kernel<<<(unsigned)((ns + threads - 1) / threads), threads, 0, stream>>>(
-      scales_a, scales_b, num_experts, rows, K / group_size, packed_scales, paired);
+      scales_a, scales_b, num_experts, rows, K, group_size, sbb, packed, paired);
   return cuda_status(cudaGetLastError());
 }
 
@@ -262,8 +272,8 @@ extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int
   return run_grouped_gemm(p, stream);
 }
 
-extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
-                                       const uint16_t* packed_scales, int N, int group_size,
+extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed, int N,
+                                       int group_size,
                                        const void* expert_offsets, int offsets_are_int64, int num_experts,
                                        const int32_t* segment_expert, int epilogue, const int32_t* dest_rows,
                                        const float* row_scale,
@@ -271,8 +281,8 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
                                        size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1);
-  LMOE_ARG_CHECK(input && packed && packed_scales && expert_offsets && output);
-  LMOE_ARG_CHECK(aligned16(input) && aligned16(packed) && aligned16(packed_scales));
+  LMOE_ARG_CHECK(input && packed && expert_offsets && output);
+  LMOE_ARG_CHECK(aligned16(input) && aligned16(packed));
   LMOE_ARG_CHECK(epilogue >= kModePlain && epilogue <= kModeScatter);
   LMOE_ARG_CHECK(ldo >= (epilogue == kModeSwiGLU ? N / 2 : N));
   if (!workspace || workspace_bytes < 256) return LMOE_ERR_WORKSPACE;
@@ -287,7 +297,6 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
   p.num_experts = num_experts;
   p.seg_expert = segment_expert;
   p.wq = packed;
-  p.wscale = packed_scales;
   p.group_size = group_size;
   p.N = N;
   p.mode = epilogue;
@@ -324,8 +333,8 @@ extern "C" size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_
 
 extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidden_size, const void* gate_weight,
                                     const float* gate_bias, int num_experts, int top_k, int num_shared,
-                                    const uint8_t* w13_packed, const uint16_t* w13_scales, const uint8_t* w2_packed,
-                                    const uint16_t* w2_scales, int ffn_size, int group_size, void* y,
+                                    const uint8_t* w13_packed, const uint8_t* w2_packed, int ffn_size, int group_size,
+                                    void* y,
                                     int32_t* ids_out, float* weights_out, void* workspace, size_t workspace_bytes,
                                     lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
@@ -333,8 +342,9 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   const int d = hidden_size, E = num_experts, k = top_k, S = num_shared, F = ffn_size;
   LMOE_ARG_CHECK(T >= 0 && d > 0 && F > 0 && E >= 1 && k >= 1 && S >= 0);
   LMOE_ARG_CHECK(E + S <= kMaxGemmExperts);
-  LMOE_ARG_CHECK(d % 128 == 0 && F % 64 == 0 && group_size % 64 == 0 && d % group_size == 0 && F % group_size == 0);
-  LMOE_ARG_CHECK(x && gate_weight && w13_packed && w13_scales && w2_packed && w2_scales && y);
+  LMOE_ARG_CHECK(d % 128 == 0 && F % 128 == 0 && group_size % 64 == 0 && d % group_size == 0 && F % group_size == 0);
+  LMOE_ARG_CHECK(group_size >= kW4SuperK || kW4SuperK % group_size == 0);
+  LMOE_ARG_CHECK(x && gate_weight && w13_packed && w2_packed && y);
   const LayerWs L = layer_ws(T, d, F, E, k, S);
   if (!workspace || workspace_bytes < L.total || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
   if (T == 0) return LMOE_OK;
@@ -377,7 +387,6 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   g1.offsets = offx;
   g1.num_experts = E + S;
   g1.wq = w13_packed;
-  g1.wscale = w13_scales;
   g1.group_size = group_size;
   g1.N = 2 * F;
   g1.mode = kModeSwiGLU;
@@ -395,7 +404,6 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   g2.offsets = offx;
   g2.num_experts = E + S;
   g2.wq = w2_packed;
-  g2.wscale = w2_scales;
   g2.group_size = group_size;
   g2.N = d;
   g2.mode = kModeScatter;

@@ -118,10 +118,10 @@ class CudaExpertBackend:
 
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         e = self.ex
-        h = ops.w4a16_grouped_gemm(rows, e.w13_packed, e.w13_scales, seg_offsets, num_seg, 2 * e.ffn_size,
-                                   e.group_size, 1, None, None, 0, max_rows, seg_expert)
-        return ops.w4a16_grouped_gemm(h, e.w2_packed, e.w2_scales, seg_offsets, num_seg, e.hidden_size,
-                                      e.group_size, 0, None, None, 0, max_rows, seg_expert)
+        h = ops.w4a16_grouped_gemm(rows, e.w13_packed, seg_offsets, num_seg, 2 * e.ffn_size, e.group_size, 1,
+                                   None, None, 0, max_rows, seg_expert)
+        return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
+                                      None, None, 0, max_rows, seg_expert)
 
     def combine(self, rows, positions, weights, T, extra, num_extra):
         return ops.combine_rows(rows, positions, weights, T, self.top_k, extra, num_extra)
@@ -216,9 +216,8 @@ def slice_experts(ex: W4A16Experts, e0: int, e1: int) -> W4A16Experts:
         return torch.cat([t[i * per:(i + 1) * per] for i in idx]) if idx else t[:0]
 
     idx = list(range(e0, e1)) + list(range(ex.num_experts, Et))
-    return W4A16Experts(part(ex.w13_packed, idx), part(ex.w13_scales, idx), part(ex.w2_packed, idx),
-                        part(ex.w2_scales, idx), e1 - e0, ex.num_shared, ex.hidden_size, ex.ffn_size,
-                        ex.group_size, None)
+    return W4A16Experts(part(ex.w13_packed, idx), part(ex.w2_packed, idx), e1 - e0, ex.num_shared,
+                        ex.hidden_size, ex.ffn_size, ex.group_size, None)
 
 
 def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):

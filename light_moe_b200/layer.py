@@ -22,10 +22,8 @@ from . import ops
 class W4A16Experts:
     """Prepacked int4 experts: ``num_experts`` routed experts followed by ``num_shared``."""
 
-    w13_packed: torch.Tensor
-    w13_scales: torch.Tensor
-    w2_packed: torch.Tensor
-    w2_scales: torch.Tensor
+    w13_packed: torch.Tensor   # paired gate/up super-blocks, scales embedded
+    w2_packed: torch.Tensor    # down super-blocks, scales embedded
     num_experts: int
     num_shared: int
     hidden_size: int
@@ -59,10 +57,10 @@ class W4A16Experts:
         """From canonical int4 tensors (routed experts first, then shared ones)."""
         Et, F, d2 = q1.shape
         d = d2 * 2
-        w13p, w13s = ops.prepack_w4(q1, s1, group_size, q3, s3)
-        w2p, w2s = ops.prepack_w4(q2, s2, group_size)
+        w13p = ops.prepack_w4(q1, s1, group_size, q3, s3)
+        w2p = ops.prepack_w4(q2, s2, group_size)
         canon = dict(q1=q1, s1=s1, q3=q3, s3=s3, q2=q2, s2=s2) if keep_canonical else None
-        return cls(w13p, w13s, w2p, w2s, num_experts, Et - num_experts, d, F, group_size, canon)
+        return cls(w13p, w2p, num_experts, Et - num_experts, d, F, group_size, canon)
 
 
 class W4A16MoELayer(torch.nn.Module):
@@ -82,8 +80,7 @@ class W4A16MoELayer(torch.nn.Module):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
         e = self.experts
-        y, ids, w = ops.moe_layer_w4a16(x2, self.gate_weight, e.w13_packed, e.w13_scales, e.w2_packed,
-                                        e.w2_scales, self.top_k, e.ffn_size, e.group_size, e.num_shared,
-                                        self.gate_bias)
+        y, ids, w = ops.moe_layer_w4a16(x2, self.gate_weight, e.w13_packed, e.w2_packed, self.top_k,
+                                        e.ffn_size, e.group_size, e.num_shared, self.gate_bias)
         y = y.view(*shape[:-1], shape[-1])
         return (y, ids, w) if return_routing else y

@@ -64,15 +64,16 @@ def dequantize_w4(qweight, scales, group_size):
 
 
 def prepack_w4(qweight, scales, group_size, qweight_up=None, scales_up=None):
-    """Canonical int4 [E, N, K/2] -> the GEMM's streaming layout (paired with up if given)."""
+    """Canonical int4 [E, N, K/2] + scales -> the GEMM's streaming layout (scales embedded;
+    paired with the up projection if given).  Returns one uint8 tensor."""
     return extension().prepack_w4(qweight, scales, group_size, qweight_up, scales_up)
 
 
-def w4a16_grouped_gemm(input, packed, packed_scales, expert_offsets, num_experts, N, group_size,
+def w4a16_grouped_gemm(input, packed, expert_offsets, num_experts, N, group_size,
                        epilogue=0, dest_rows=None, row_scale=None, out_rows=0, max_rows_per_expert=0,
                        segment_expert=None):
     """Grouped W4A16 GEMM over `num_experts` row segments (segment_expert maps segment -> weights)."""
-    return extension().w4a16_grouped_gemm(input, packed, packed_scales, expert_offsets, num_experts, N,
+    return extension().w4a16_grouped_gemm(input, packed, expert_offsets, num_experts, N,
                                           group_size, epilogue, dest_rows, row_scale, out_rows,
                                           max_rows_per_expert, segment_expert)
 
@@ -82,8 +83,8 @@ def combine_rows(rows, positions, weights, num_tokens, top_k, extra_rows=None, n
     return extension().combine_rows(rows, positions, weights, num_tokens, top_k, extra_rows, num_extra)
 
 
-def moe_layer_w4a16(x, gate_weight, w13_packed, w13_scales, w2_packed, w2_scales, top_k, ffn_size,
-                    group_size, num_shared=0, gate_bias=None):
+def moe_layer_w4a16(x, gate_weight, w13_packed, w2_packed, top_k, ffn_size, group_size, num_shared=0,
+                    gate_bias=None):
     """[y bf16 [T, d], ids int32 [T, k], weights fp32 [T, k]]."""
-    return extension().moe_layer_w4a16(x, gate_weight, w13_packed, w13_scales, w2_packed, w2_scales, top_k,
-                                       ffn_size, group_size, num_shared, gate_bias)
+    return extension().moe_layer_w4a16(x, gate_weight, w13_packed, w2_packed, top_k, ffn_size, group_size,
+                                       num_shared, gate_bias)

@@ -72,17 +72,14 @@ def prepack(q, s, group_size, q_up=None, s_up=None):
     E, N, K2 = q.shape
     K = K2 * 2
     pb = ctypes.c_size_t()
-    sb = ctypes.c_size_t()
-    capi.call("lmoe_w4_prepacked_sizes", E, N, K, group_size, 1 if q_up is not None else 0, ctypes.byref(pb),
-              ctypes.byref(sb))
+    capi.call("lmoe_w4_prepacked_bytes", E, N, K, group_size, 1 if q_up is not None else 0, ctypes.byref(pb))
     packed = torch.empty(pb.value, dtype=torch.uint8, device=q.device)
-    pscale = torch.empty(sb.value // 2, dtype=torch.float16, device=q.device)
     capi.call("lmoe_prepack_w4", q.data_ptr(), s.data_ptr(), capi.ptr(q_up), capi.ptr(s_up), E, N, K, group_size,
-              packed.data_ptr(), pscale.data_ptr(), stream())
-    return packed, pscale
+              packed.data_ptr(), stream())
+    return packed
 
 
-def w4_gemm(x, packed, pscale, N, group_size, offsets, epilogue=0, dest=None, row_scale=None, out_rows=None,
+def w4_gemm(x, packed, N, group_size, offsets, epilogue=0, dest=None, row_scale=None, out_rows=None,
             hint=0, seg_expert=None):
     R, K = x.shape
     E = offsets.numel() - 1
@@ -90,7 +87,7 @@ def w4_gemm(x, packed, pscale, N, group_size, offsets, epilogue=0, dest=None, ro
     rows_out = out_rows if out_rows is not None else R
     out = torch.zeros(rows_out, ncols, dtype=torch.bfloat16, device=x.device)
     ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
-    capi.call("lmoe_w4a16_grouped_gemm", x.data_ptr(), R, K, packed.data_ptr(), pscale.data_ptr(), N, group_size,
+    capi.call("lmoe_w4a16_grouped_gemm", x.data_ptr(), R, K, packed.data_ptr(), N, group_size,
               offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, capi.ptr(seg_expert), epilogue,
               capi.ptr(dest),
               capi.ptr(row_scale), hint, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), stream())
@@ -123,8 +120,7 @@ def layer(x, gate_w, experts, top_k, gate_bias=None):
     nbytes = capi.lib().lmoe_moe_layer_workspace_bytes(T, d, e.ffn_size, E, top_k, e.num_shared)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     capi.call("lmoe_moe_layer_w4a16", x.data_ptr(), T, d, gate_w.data_ptr(), capi.ptr(gate_bias), E, top_k,
-              e.num_shared, e.w13_packed.data_ptr(), e.w13_scales.data_ptr(), e.w2_packed.data_ptr(),
-              e.w2_scales.data_ptr(), e.ffn_size, e.group_size, y.data_ptr(), ids.data_ptr(), wts.data_ptr(),
+              e.num_shared, e.w13_packed.data_ptr(), e.w2_packed.data_ptr(), e.ffn_size, e.group_size, y.data_ptr(), ids.data_ptr(), wts.data_ptr(),
               ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     assert read_error(ws) == 0

@@ -64,7 +64,7 @@ def _check(y, ref):
     assert err <= TOL * scale, f"max rel err {err / scale:.3e}"
 
 
-@pytest.mark.parametrize("T,d,F,E,k,g", [(64, 256, 256, 8, 2, 128), (200, 128, 192, 16, 4, 64), (5, 256, 256, 8, 2, 128)])
+@pytest.mark.parametrize("T,d,F,E,k,g", [(64, 256, 256, 8, 2, 128), (200, 128, 256, 16, 4, 64), (5, 256, 256, 8, 2, 128)])
 def test_layer_matches_cpu_oracle(T, d, F, E, k, g):
     x, gw, ex, _ = _make(T, d, F, E, k, g, seed=T)
     y, ids, wts = layer(x, gw, ex, k)

@@ -51,10 +51,10 @@ def _expert_setup(E, N, K, g, seed, paired=False):
         w3 = _w((E, N, K), seed + 1)
         q3, s3 = quantize(w3, g)
         deq3 = dequantize(q3, s3, g).float()
-        packed, pscale = prepack(q, s, g, q3, s3)
-        return packed, pscale, deq, deq3
-    packed, pscale = prepack(q, s, g)
-    return packed, pscale, deq
+        packed = prepack(q, s, g, q3, s3)
+        return packed, deq, deq3
+    packed = prepack(q, s, g)
+    return packed, deq
 
 
 def _offsets(counts, dtype=torch.int32):
@@ -85,12 +85,12 @@ def _assert_close(y, ref):
 def test_gemm_dequant_bitexact_via_identity(K, g):
     """X = identity rows: Y[r, n] = W_deq[n, r] exactly (fp32 accumulation of one term)."""
     E, N = 2, 256
-    packed, pscale, deq = _expert_setup(E, N, K, g, seed=K)
+    packed, deq = _expert_setup(E, N, K, g, seed=K)
     rows = min(K, 512)
     eye = torch.eye(K, dtype=torch.bfloat16, device="cuda")[:rows]
     x = torch.cat([eye, eye])                       # expert 0 and expert 1 see the same rows
     off = _offsets([rows, rows])
-    y = w4_gemm(x, packed, pscale, N, g, off)
+    y = w4_gemm(x, packed, N, g, off)
     want0 = deq[0][:, :rows].T.to(torch.bfloat16)
     want1 = deq[1][:, :rows].T.to(torch.bfloat16)
     assert np.array_equal(bf16_bits(y[:rows]), bf16_bits(want0))
@@ -105,11 +105,11 @@ def test_gemm_dequant_bitexact_via_identity(K, g):
 ])
 def test_w4_gemm_plain(counts, hint):
     E, N, K, g = len(counts), 384, 512, 128
-    packed, pscale, deq = _expert_setup(E, N, K, g, seed=sum(counts))
+    packed, deq = _expert_setup(E, N, K, g, seed=sum(counts))
     R = sum(counts)
     x = _w((R, K), seed=R, scale=1.0)
     off = _offsets(counts)
-    y = w4_gemm(x, packed, pscale, N, g, off, hint=hint)
+    y = w4_gemm(x, packed, N, g, off, hint=hint)
     _assert_close(y, _ref_plain(x, deq, off))
 
 
@@ -119,22 +119,22 @@ def test_w4_gemm_many_experts_int64_offsets():
     counts = rng.zipf(1.5, E).clip(0, 400)
     counts[::7] = 0
     N, K, g = 256, 1024, 64
-    packed, pscale, deq = _expert_setup(E, N, K, g, seed=5)
+    packed, deq = _expert_setup(E, N, K, g, seed=5)
     R = int(counts.sum())
     x = _w((R, K), seed=9, scale=1.0)
     off = _offsets(counts, torch.int64)
-    y = w4_gemm(x, packed, pscale, N, g, off)
+    y = w4_gemm(x, packed, N, g, off)
     _assert_close(y, _ref_plain(x, deq, off))
 
 
 @pytest.mark.parametrize("counts,hint", [([200, 0, 64, 9], 0), ([3, 16, 40, 64], 64)])
 def test_w4_gemm_swiglu(counts, hint):
     E, F, K, g = len(counts), 320, 512, 128
-    packed, pscale, d1, d3 = _expert_setup(E, F, K, g, seed=3, paired=True)
+    packed, d1, d3 = _expert_setup(E, F, K, g, seed=3, paired=True)
     R = sum(counts)
     x = _w((R, K), seed=4, scale=1.0)
     off = _offsets(counts)
-    h = w4_gemm(x, packed, pscale, 2 * F, g, off, epilogue=1, hint=hint)
+    h = w4_gemm(x, packed, 2 * F, g, off, epilogue=1, hint=hint)
     gate = _ref_plain(x, d1, off)
     up = _ref_plain(x, d3, off)
     ref = torch.nn.functional.silu(gate) * up
@@ -144,13 +144,13 @@ def test_w4_gemm_swiglu(counts, hint):
 def test_w4_gemm_scatter():
     counts = [50, 0, 33, 77]
     E, N, K, g = 4, 256, 256, 64
-    packed, pscale, deq = _expert_setup(E, N, K, g, seed=8)
+    packed, deq = _expert_setup(E, N, K, g, seed=8)
     R = sum(counts)
     x = _w((R, K), seed=2, scale=1.0)
     off = _offsets(counts)
     perm = torch.randperm(R + 10, device="cuda")[:R].to(torch.int32)
     scale = torch.rand(R, device="cuda")
-    y = w4_gemm(x, packed, pscale, N, g, off, epilogue=2, dest=perm, row_scale=scale, out_rows=R + 10)
+    y = w4_gemm(x, packed, N, g, off, epilogue=2, dest=perm, row_scale=scale, out_rows=R + 10)
     ref = torch.zeros(R + 10, N, device="cuda")
     ref[perm.long()] = _ref_plain(x, deq, off) * scale[:, None]
     _assert_close(y, ref)
