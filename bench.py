@@ -172,7 +172,7 @@ def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
                 "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
     achieved = bytes_ / secs / 1e9
     peak = peaks["hbm_gbs"]
-    return {"kernel": "grouped_gemm_kernel<64,...,W4> gate/up+SwiGLU", "bound": "hbm",
+    return {"kernel": "w4_decode_kernel gate/up+SwiGLU", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
             "peak_source": f"{peak_kind} HBM copy", "launch_us": round(secs * 1e6, 1),
             "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}

@@ -134,15 +134,20 @@ __device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_
 __device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __nv_bfloat162 bits_bf16x2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
 
-// Dequantise one interleaved word (8 K values) into 4 bf16x2 registers.
-__device__ __forceinline__ void dequant_word(uint32_t w, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo,
-                                             const __nv_bfloat162 off136, uint32_t* out4) {
+// Dequantise one 16-byte half-row (32 K values, w4_layout.cuh) into the 16 bf16x2 registers
+// of its K pairs in order: pair m = 4i + c lives in word c, slot i.
+__device__ __forceinline__ void dequant_half(const uint4 v, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo,
+                                             const __nv_bfloat162 off136, uint32_t (&o)[16]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const uint32_t x = ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;   // bf16 pair (128 + u)
-    const __nv_bfloat162 q = __hsub2(bits_bf16x2(x), off136);           // exact q = u - 8
-    const __nv_bfloat162 t = __hmul2(q, s_lo);                           // exact (<= 6 bits)
-    out4[p] = bf16x2_bits(__hfma2(q, s_hi, t));                          // one rounding of q*s
+  for (int c = 0; c < 4; ++c) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t x = ((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16 pair (128 + u)
+      const __nv_bfloat162 q = __hsub2(bits_bf16x2(x), off136);            // exact q = u - 8
+      const __nv_bfloat162 t = __hmul2(q, s_lo);                            // exact (<= 6 bits)
+      o[4 * i + c] = bf16x2_bits(__hfma2(q, s_hi, t));                      // one rounding of q*s
+    }
   }
 }
 
@@ -366,11 +371,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
             split_scale(j == 0 ? sb0 : sb1, s_hi, s_lo);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint4 w4 = v[2 * j + h];
-              dequant_word(w4.x, s_hi, s_lo, off136, &o[2 * j + h][0]);
-              dequant_word(w4.y, s_hi, s_lo, off136, &o[2 * j + h][4]);
-              dequant_word(w4.z, s_hi, s_lo, off136, &o[2 * j + h][8]);
-              dequant_word(w4.w, s_hi, s_lo, off136, &o[2 * j + h][12]);
+              dequant_half(v[2 * j + h], s_hi, s_lo, off136, o[2 * j + h]);
             }
           }
           if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
@@ -388,11 +389,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               uint32_t o[16];
-              const uint4 w4 = v[2 * j + h];
-              dequant_word(w4.x, s_hi, s_lo, off136, &o[0]);
-              dequant_word(w4.y, s_hi, s_lo, off136, &o[4]);
-              dequant_word(w4.z, s_hi, s_lo, off136, &o[8]);
-              dequant_word(w4.w, s_hi, s_lo, off136, &o[12]);
+              dequant_half(v[2 * j + h], s_hi, s_lo, off136, o);
               tmem_st16(taddr + (2 * j + h) * 16, o);
             }
           }

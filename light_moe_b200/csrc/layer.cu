@@ -14,6 +14,7 @@
 // SparseMoEBlockFast.forward (moe_block.py:216-274).
 #include <cuda_bf16.h>
 
+#include "decode_gemm.h"
 #include "grouped_gemm.h"
 #include "host_util.h"
 #include "ptx.cuh"
@@ -49,11 +50,7 @@ __global__ void prepack_w4_kernel(const uint8_t* __restrict__ qa, const uint8_t*
   const int64_t srow = prepack_src_row(e, rows_in, fb, r, paired);
   const int k0 = sb * kW4SuperK + (jh >> 1) * 64 + (jh & 1) * 32;
   const uint4 c = *reinterpret_cast<const uint4*>(src + srow * (K / 2) + k0 / 2);
-  uint4 o;
-  o.x = w4_interleave_word(c.x);
-  o.y = w4_interleave_word(c.y);
-  o.z = w4_interleave_word(c.z);
-  o.w = w4_interleave_word(c.w);
+  const uint4 o = w4_device_half(c);
   uint8_t* dst = out + ((int64_t)(e * NB + fb) * KSB + sb) * sb_bytes + jh * 2048 + r * 16;
   *reinterpret_cast<uint4*>(dst) = o;
 }
@@ -168,11 +165,50 @@ __global__ void combine_rows_kernel(const __nv_bfloat162* __restrict__ rows, con
   y[i] = __floats2bfloat162_rn(ax, ay);
 }
 
+// Decode path: y[t, :] = sum_j w[t*k+j] * P(pos[t*k+j]) + sum_s P(Rr + s*T + t), where
+// P(r) = sum over the K chunks c of part[c][r, :] (fp32, chunk order fixed).
+__global__ void combine_partials_kernel(const float* __restrict__ part, int ksplit, int64_t R,
+                                        const int32_t* __restrict__ pos, const float* __restrict__ w, int64_t T,
+                                        int k, int S, int d, __nv_bfloat16* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * d) return;
+  const int64_t t = i / d;
+  const int c = (int)(i - t * d);
+  const int64_t Rr = T * k;
+  float acc = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    const int64_t r = pos[t * k + j];
+    float v = 0.0f;
+    for (int q = 0; q < ksplit; ++q) v = __fadd_rn(v, part[((int64_t)q * R + r) * d + c]);
+    acc = __fadd_rn(acc, __fmul_rn(w[t * k + j], v));
+  }
+  for (int s2 = 0; s2 < S; ++s2) {
+    const int64_t r = Rr + (int64_t)s2 * T + t;
+    float v = 0.0f;
+    for (int q = 0; q < ksplit; ++q) v = __fadd_rn(v, part[((int64_t)q * R + r) * d + c]);
+    acc = __fadd_rn(acc, v);
+  }
+  y[i] = __float2bfloat16_rn(acc);
+}
+
+// K chunks for the decode down projection: the smallest divisor of the stage count that gives
+// at least ~8 tiles per SM, so the tail of the static schedule stays short.
+inline int pick_ksplit(int KS, int64_t tiles_per_chunk, int num_sms) {
+  for (int d = 1; d <= KS && d <= 16; ++d)
+    if (KS % d == 0 && tiles_per_chunk * d >= 8LL * num_sms) return d;
+  int best = 1;
+  for (int d = 1; d <= KS && d <= 16; ++d)
+    if (KS % d == 0) best = d;
+  return best;
+}
+
+constexpr int kDecodeMaxSplit = 16;
+
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Workspace carve-up of the layer (all 256-byte aligned).
 struct LayerWs {
-  size_t router, ids, wts, counts, offs, sidx, src, dest, scale, offx, xp, h, o, total;
+  size_t router, ids, wts, counts, offs, sidx, pos, src, dest, scale, offx, xp, h, o, part, total;
 };
 
 LayerWs layer_ws(int64_t T, int d, int ffn, int E, int k, int S) {
@@ -188,6 +224,7 @@ LayerWs layer_ws(int64_t T, int d, int ffn, int E, int k, int S) {
   w.counts = p; p = align256(p + sizeof(int32_t) * E);
   w.offs = p; p = align256(p + sizeof(int32_t) * (E + 1));
   w.sidx = p; p = align256(p + sizeof(int32_t) * T * k);
+  w.pos = p; p = align256(p + sizeof(int32_t) * T * k);
   w.src = p; p = align256(p + sizeof(int32_t) * R);
   w.dest = p; p = align256(p + sizeof(int32_t) * R);
   w.scale = p; p = align256(p + sizeof(float) * R);
@@ -195,6 +232,9 @@ LayerWs layer_ws(int64_t T, int d, int ffn, int E, int k, int S) {
   w.xp = p; p = align256(p + sizeof(uint16_t) * R * d);
   w.h = p; p = align256(p + sizeof(uint16_t) * R * ffn);
   w.o = p; p = align256(p + sizeof(uint16_t) * T * (k + S) * d);
+  // decode path (T <= 64): fp32 partial sums of the split-K down projection
+  w.part = p;
+  if (T <= kDecodeMaxRows) p = align256(p + sizeof(float) * (size_t)kDecodeMaxSplit * R * d);
   w.total = p;
   return w;
 }
@@ -306,6 +346,25 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
   p.row_scale = row_scale;
   p.err = static_cast<uint32_t*>(workspace);
   p.max_rows_per_expert_hint = max_rows_per_expert;
+  if (max_rows_per_expert > 0 && max_rows_per_expert <= kDecodeMaxRows && epilogue != kModeScatter) {
+    DecodeProblem d;
+    d.x = input;
+    d.ldx = K;
+    d.total_rows = total_rows;
+    d.K = K;
+    d.offsets = expert_offsets;
+    d.offsets_i64 = offsets_are_int64;
+    d.num_experts = num_experts;
+    d.seg_expert = segment_expert;
+    d.wq = packed;
+    d.group_size = group_size;
+    d.N = N;
+    d.mode = epilogue == kModeSwiGLU ? kDecodeSwiGLU : kDecodePlain;
+    d.out = output;
+    d.ldo = ldo;
+    d.err = p.err;
+    return run_decode_gemm(d, stream);
+  }
   return run_grouped_gemm(p, stream);
 }
 
@@ -355,6 +414,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   int32_t* counts = static_cast<int32_t*>(at(L.counts));
   int32_t* offs = static_cast<int32_t*>(at(L.offs));
   int32_t* sidx = static_cast<int32_t*>(at(L.sidx));
+  int32_t* posn = static_cast<int32_t*>(at(L.pos));
   int32_t* src = static_cast<int32_t*>(at(L.src));
   int32_t* dest = static_cast<int32_t*>(at(L.dest));
   float* scale = static_cast<float*>(at(L.scale));
@@ -363,7 +423,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   const int64_t R = T * k + (int64_t)S * T;
 
   int st = lmoe_fused_gate_topk(x, gate_weight, gate_bias, T, d, E, k, ids, wts, nullptr, counts, offs, sidx,
-                                nullptr, nullptr, at(L.router), lmoe_router_workspace_bytes(T, E), stream_);
+                                posn, nullptr, at(L.router), lmoe_router_workspace_bytes(T, E), stream_);
   if (st != LMOE_OK) return st;
   {
     const int threads = 256;
@@ -376,6 +436,47 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
     gather_rows_kernel<<<(unsigned)grid, vec >= 256 ? 256 : vec, 0, stream>>>(
         static_cast<const uint4*>(x), src, R, vec, static_cast<uint4*>(at(L.xp)));
     LMOE_CUDA_TRY(cudaGetLastError());
+  }
+  if (T <= kDecodeMaxRows) {
+    // decode: every expert holds at most T <= 64 rows -> warp-level MMA path, split-K down
+    DecodeProblem d1;
+    d1.x = at(L.xp);
+    d1.ldx = d;
+    d1.total_rows = R;
+    d1.K = d;
+    d1.offsets = offx;
+    d1.num_experts = E + S;
+    d1.wq = w13_packed;
+    d1.group_size = group_size;
+    d1.N = 2 * F;
+    d1.mode = kDecodeSwiGLU;
+    d1.out = at(L.h);
+    d1.ldo = F;
+    d1.err = err;
+    st = run_decode_gemm(d1, stream);
+    if (st != LMOE_OK) return st;
+    DeviceInfo dev;
+    st = get_device_info(&dev);
+    if (st != LMOE_OK) return st;
+    const int KS2 = F / kW4SuperK;
+    const int ksplit = pick_ksplit(KS2, (int64_t)(E + S) * (d / 128), dev.num_sms);
+    DecodeProblem d2 = d1;
+    d2.x = at(L.h);
+    d2.ldx = F;
+    d2.K = F;
+    d2.wq = w2_packed;
+    d2.N = d;
+    d2.mode = kDecodePartial;
+    d2.ksplit = ksplit;
+    d2.out = at(L.part);
+    d2.ldo = d;
+    st = run_decode_gemm(d2, stream);
+    if (st != LMOE_OK) return st;
+    const int threads = 256;
+    const int64_t n = T * d;
+    combine_partials_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+        static_cast<const float*>(at(L.part)), ksplit, R, posn, wts, T, k, S, d, static_cast<__nv_bfloat16*>(y));
+    return cuda_status(cudaGetLastError());
   }
   // a routed expert receives at most T rows; shared experts exactly T
   const int64_t hint = T;

@@ -81,20 +81,25 @@ def _assert_close(y, ref):
     assert torch.all((y.float() - ref).abs() <= ref.abs() * 2 ** -7 + 2e-3 * scale)
 
 
-@pytest.mark.parametrize("K,g", [(256, 128), (4096, 128), (2048, 64)])
-def test_gemm_dequant_bitexact_via_identity(K, g):
-    """X = identity rows: Y[r, n] = W_deq[n, r] exactly (fp32 accumulation of one term)."""
+@pytest.mark.parametrize("K,g,hint", [(256, 128, 0), (4096, 128, 0), (2048, 64, 0), (4096, 128, 64), (2048, 64, 64)])
+def test_gemm_dequant_bitexact_via_identity(K, g, hint):
+    """X = identity rows: Y[r, n] = W_deq[n, r] exactly.  hint=0 runs the tcgen05 kernel
+    (bf16 weights in tensor memory, one-term fp32 sums); hint=64 runs the decode kernel
+    (integer weights, fp32 q*s applied after the MMA, one bf16 rounding at the output)."""
     E, N = 2, 256
-    packed, deq = _expert_setup(E, N, K, g, seed=K)
-    rows = min(K, 512)
-    eye = torch.eye(K, dtype=torch.bfloat16, device="cuda")[:rows]
-    x = torch.cat([eye, eye])                       # expert 0 and expert 1 see the same rows
-    off = _offsets([rows, rows])
-    y = w4_gemm(x, packed, N, g, off)
-    want0 = deq[0][:, :rows].T.to(torch.bfloat16)
-    want1 = deq[1][:, :rows].T.to(torch.bfloat16)
-    assert np.array_equal(bf16_bits(y[:rows]), bf16_bits(want0))
-    assert np.array_equal(bf16_bits(y[rows:]), bf16_bits(want1))
+    packed, deq = _expert_setup(E, N, K, g, seed=K + hint)
+    rows = 64 if hint else min(K, 512)
+    for r0 in range(0, min(K, 512), rows):
+        eye = torch.eye(K, dtype=torch.bfloat16, device="cuda")[r0:r0 + rows]
+        x = torch.cat([eye, eye])                   # expert 0 and expert 1 see the same rows
+        off = _offsets([rows, rows])
+        y = w4_gemm(x, packed, N, g, off, hint=hint)
+        want0 = deq[0][:, r0:r0 + rows].T.to(torch.bfloat16)
+        want1 = deq[1][:, r0:r0 + rows].T.to(torch.bfloat16)
+        assert np.array_equal(bf16_bits(y[:rows]), bf16_bits(want0))
+        assert np.array_equal(bf16_bits(y[rows:]), bf16_bits(want1))
+        if not hint:
+            break
 
 
 @pytest.mark.parametrize("counts,hint", [
