@@ -77,6 +77,25 @@ int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const floa
                          int32_t* positions, float* logits,
                          void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
 
+/* lmoe_fused_gate_topk without a workspace argument (no counterpart in the reference): the
+ * scratch lives in a fixed 640 KB device array inside this library, for callers that may
+ * not allocate device memory (an allocator that owns all device memory, a serving loop that
+ * forbids allocation after start-up).
+ *   - num_tokens <= 16384 (any num_experts <= 256); larger calls return LMOE_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address; make that first call
+ *     before any stream capture.  Later calls allocate nothing.
+ *   - All calls on a device share the one array, which keeps whatever the last call left in
+ *     it (each call clears the parts that must start at zero).  Calls that overlap in time,
+ *     on different streams or host threads, race on it: serialise them.
+ *   - A wait timeout recorded by the kernel stays in the shared array; use
+ *     lmoe_fused_gate_topk with a workspace when the device error word must be read.
+ * Other arguments, outputs and status codes as lmoe_fused_gate_topk. */
+int lmoe_fused_gate_topk_static(const void* hidden, const void* gate_weight, const float* gate_bias,
+                                int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                                int32_t* ids, float* weights, void* weights_bf16,
+                                int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
+                                int32_t* positions, float* logits, lmoe_stream_t stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Row gather / weighted combine                                                          */
 /* ------------------------------------------------------------------------------------ */

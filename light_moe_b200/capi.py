@@ -31,6 +31,7 @@ SIGNATURES = {
     "lmoe_read_error": (_I, [_P, _P, _P]),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_fused_gate_topk": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "lmoe_fused_gate_topk_static": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lmoe_permute_rows": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "lmoe_quantize_w4": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P]),
     "lmoe_dequantize_w4": (_I, [_P, _P, _I64, _I, _I, _P, _P]),

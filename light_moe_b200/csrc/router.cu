@@ -24,6 +24,8 @@
 // barrier, every CTA scans the per-tile counts and scatters its tokens into sorted_idx.
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "host_util.h"
 #include "lmoe_math.cuh"
 #include "ptx.cuh"
@@ -367,6 +369,41 @@ int launch_router(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const Router
   return cuda_status(cudaLaunchKernelEx(&cfg, fn, tm_x, tm_w, a));
 }
 
+// ---------------------------------------------------------------------------------------
+// Router scratch in a fixed device array, for lmoe_fused_gate_topk_static: callers that may
+// not allocate device memory at all (a custom allocator that owns every byte, a serving
+// loop that forbids allocation after start-up) get the router without passing a workspace.
+// Limits: at most kStaticMaxTokens tokens per call (num_experts <= 256 always fits).
+// ---------------------------------------------------------------------------------------
+constexpr int64_t kStaticMaxTokens = 16384;
+constexpr size_t kStaticScratchBytes =
+    ((256 + (size_t)((kStaticMaxTokens + kBM - 1) / kBM) * kMaxExperts * sizeof(int32_t) + 255) & ~size_t(255)) +
+    (size_t)((kStaticMaxTokens + kBM - 1) / kBM) * kMaxExperts * 4 * sizeof(uint32_t);   // 640 KB + 256 B
+
+static __device__ __align__(256) uint8_t g_router_scratch[kStaticScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
+// Device address of g_router_scratch on the current device, looked up once per device (the
+// first call on a device does the lookup; later calls only read the cached pointer).
+int router_scratch(void** out) {
+  int dev = 0;
+  LMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxScratchDevices) return LMOE_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (!p) return LMOE_ERR_DEVICE;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return LMOE_OK;
+}
+
 }  // namespace
 }  // namespace lmoe
 
@@ -472,4 +509,21 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   if (top_k <= 4) return launch_router<4>(tm_x, tm_w, a, grid, smem, stream);
   if (top_k <= 8) return launch_router<8>(tm_x, tm_w, a, grid, smem, stream);
   return launch_router<16>(tm_x, tm_w, a, grid, smem, stream);
+}
+
+extern "C" int lmoe_fused_gate_topk_static(const void* hidden, const void* gate_weight, const float* gate_bias,
+                                           int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                                           int32_t* ids, float* weights, void* weights_bf16, int32_t* counts,
+                                           int32_t* offsets, int32_t* sorted_idx, int32_t* positions,
+                                           float* logits, lmoe_stream_t stream) {
+  if (num_tokens > kStaticMaxTokens) return LMOE_ERR_WORKSPACE;   // beyond the fixed scratch
+  static_assert(kStaticScratchBytes % 256 == 0, "scratch size");
+  void* scratch = nullptr;
+  const int st = router_scratch(&scratch);
+  if (st != LMOE_OK) return st;
+  // same kernel and checks as the workspace entry point; the scratch header (error word and
+  // grid barrier) is cleared there on the stream before every launch
+  return lmoe_fused_gate_topk(hidden, gate_weight, gate_bias, num_tokens, hidden_size, num_experts, top_k, ids,
+                              weights, weights_bf16, counts, offsets, sorted_idx, positions, logits, scratch,
+                              kStaticScratchBytes, stream);
 }
