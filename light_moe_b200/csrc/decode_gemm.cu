@@ -20,15 +20,16 @@
 //     sum_k (q * s) * x up to fp32 rounding (it never rounds the weights to bf16).
 //
 //   * a tcgen05.commit costs about as much issue time as an MMA, and an mbarrier wait in
-//     the issuing thread about three times that, so an issuer does one wait, its four MMAs
-//     and one commit per stage.  The q stage, the token stage and the partial-sum slot
-//     share one ring index; "stage ready" (a_full) collects the dequantisers' arrivals,
-//     the token TMA bytes and the epilogue's release of the slot's previous round, and
-//     "stage done" (mma_done) collects both issuers' commits and the dequantisers'
-//     "scales written" arrivals, so the epilogue also waits once per stage.
+//     the issuing thread ~270 cycles even when the phase has long completed, so an issuer
+//     polls a shared-memory counter (published by warp 16 after its barrier wait), issues
+//     its four MMAs and commits once per stage.  The q stage, the token stage and the
+//     partial-sum slot share one ring index; "stage ready" (a_full) collects the
+//     dequantisers' arrivals, the token TMA bytes and the epilogue's release of the slot's
+//     previous round, and "stage done" (mma_done) collects both issuers' commits and the
+//     dequantisers' "scales written" arrivals, so the epilogue also waits once per stage.
 //
 // CTA = one 128-row weight block x up to 32 tokens of one segment (x one K chunk when
-// split-K is used), streamed in 128-K stages.  Warp roles (512 threads, one CTA per SM):
+// split-K is used), streamed in 128-K stages.  Warp roles (544 threads, one CTA per SM):
 //   warp 0        token producer: two TMA boxes (16 or 32 rows x 64 K) per stage
 //   warp 1        weight producer: one bulk copy of the int4 super-block per stage
 //   warps 2, 3    MMA issuers for k-block 0 / 1 of every stage (tcgen05 "TS": A = q from
@@ -39,6 +40,9 @@
 //                 2 x kRing slots (a slot is rewritten only after the epilogue has released
 //                 the partial sums of the round before)
 //   warps 12..15  epilogue: partial sums -> registers (scaled), output at the tile end
+//   warp 16       waits on the stage-ready barrier for the issuers and publishes a counter
+//                 they poll (an mbarrier wait in an MMA-issuing thread costs ~270 cycles,
+//                 a shared-memory load ~40)
 // Epilogues: SwiGLU (gate rows 0..63 / up rows 64..127 of the paired layout), plain bf16,
 // or fp32 partial sums per K chunk for split-K (reduced in a fixed order by the combine
 // kernel, so results are deterministic).
@@ -61,7 +65,8 @@ constexpr int kWST = 16;             // int4 super-block stages (shared memory)
 constexpr int kRing = 4;             // q (tensor memory, 64 columns), token (shared memory) and
                                      // partial-sum (tensor memory, 2 x kBN columns) stages
 constexpr int kWarpX = 0, kWarpW = 1, kWarpM0 = 2, kWarpDQ = 4, kWarpEpi = kWarpDQ + kDQ;
-constexpr int kThreads = (kWarpEpi + 4) * 32;
+constexpr int kWarpSync = kWarpEpi + 4;   // waits on a_full for the issuers
+constexpr int kThreads = (kWarpSync + 1) * 32;
 constexpr uint32_t kBStageBytes = 2u * kBN * 64 * 2;          // [2 k-blocks][32 tokens][64] bf16, SW128
 constexpr uint32_t kWStageBytes = kW4SuperInt4Bytes + 512;    // int4 + up to two scale groups
 constexpr uint32_t kXchgBytes = 64 * (kBN + 1) * 4;           // SwiGLU exchange [64 rows][33]
@@ -72,8 +77,8 @@ constexpr uint32_t kSite = 0x300u;
 static_assert(kTmemP + kRing * 2 * kBN <= kTmemCols, "tensor memory budget");
 static_assert(kWST % kGroups == 0 && kRing % kGroups == 0, "every stage has one owning dequantiser group");
 // Parity waits are exact only while a waiter is at most one phase behind its barrier:
-//   a_full[s]   (issuers)  -- the next round needs the epilogue's release of this round,
-//               which needs this round's MMAs
+//   a_full[s]   (warp 16, for the issuers) -- the next round needs the epilogue's release of
+//               this round, which needs this round's MMAs, issued after warp 16 published
 //   mma_done[s] (epilogue) -- the next round's MMAs need the epilogue's release;
 //               (dequantisers, token producer, waiting for the previous round) -- this
 //               round needs their own arrivals
@@ -101,6 +106,7 @@ struct __align__(8) DecodeBars {
                                // bytes), previous round's partial sums read (4 epilogue warps)
   uint64_t mma_done[kRing];    // both issuers' MMAs finished (2 commits), scales written (4)
   uint64_t done[2];
+  uint32_t ready;              // stages whose a_full phase has completed (published by kWarpSync)
   uint32_t tmem_base;
   int abort;
   int total_tiles;
@@ -185,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->done[0], 1);
     mbar_init(&bars->done[1], 1);
     bars->abort = 0;
+    bars->ready = 0;
     fence_mbar_init();
     // the epilogue's share of every slot's first round: there is no earlier round to release
     for (int s = 0; s < kRing; ++s)
@@ -288,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t idesc = idesc_bf16_f32(kBM, (uint32_t)((t.rows + 15) & ~15));
         for (int ks = 0; ks < ks_per; ++ks, ++it) {
           const int s = it % kRing;
-          if (!mbar_wait(&bars->a_full[s], (it / kRing) & 1u, a.err, abort_flag, kSite + 5)) {
+          if (!counter_wait(&bars->ready, it, a.err, abort_flag, kSite + 5)) {
             ok = false;
             break;
           }
@@ -304,6 +311,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&bars->done[kb]);
       mbar_wait(&bars->done[kb], 0, a.err, nullptr, kSite + 8);
+    }
+  } else if (warp == kWarpSync) {
+    // ------------------------------------------------------------------ issuers' waiter
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        for (int ks = 0; ks < ks_per; ++ks, ++it) {
+          if (!mbar_wait(&bars->a_full[it % kRing], (it / kRing) & 1u, a.err, abort_flag, kSite + 14)) {
+            ok = false;
+            break;
+          }
+          st_release_shared(&bars->ready, it + 1);
+        }
+      }
     }
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------------ dequantisers

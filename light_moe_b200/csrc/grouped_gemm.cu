@@ -23,11 +23,14 @@
 //
 // Warp roles (one CTA per SM, persistent over a static round-robin tile schedule):
 //   warp 0            token-tile producer (TMA)
-//   warp 1            MMA issuer (one thread)
+//   warp 1            MMA issuer (one thread) for token columns [0, BN/2) of every tile
 //   warp 2            weight producer (bulk copy of int4 super-blocks / TMA of bf16 tiles)
 //   warps 3..3+DQ-1   int4 dequantisers (W4 only), DQ/4 groups of 4 warps; a group owns
 //                     every (DQ/4)-th stage, one weight row per thread
-//   last 4 warps      epilogue: TMEM -> registers -> (SwiGLU | scale+scatter) -> global
+//   next 4 warps      epilogue: TMEM -> registers -> (SwiGLU | scale+scatter) -> global
+//   next warp         the MMA issuers' waiter: waits on the stage and accumulator barriers
+//                     and publishes a counter the issuers poll
+//   last warp         second MMA issuer, token columns [BN/2, BN)
 // Every stage covers 128 K values (two 64-wide swizzle atoms), so each mbarrier wait,
 // expect-tx and commit is amortised over eight 128 x N x 16 MMAs, and the two producers
 // issue their copies in parallel.
@@ -44,6 +47,7 @@
 #include "grouped_gemm.h"
 #include "host_util.h"
 #include "ptx.cuh"
+#include "w4_dequant.cuh"
 #include "w4_layout.cuh"
 
 namespace lmoe {
@@ -76,7 +80,9 @@ struct Cfg {
   static constexpr int kDQWarps = W4 ? DQ : 0;
   static constexpr int kGroups = W4 ? DQ / 4 : 1;
   static constexpr int kEpiWarp0 = 3 + kDQWarps;
-  static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
+  static constexpr int kWaitWarp = kEpiWarp0 + 4;
+  static constexpr int kIssue2Warp = kWaitWarp + 1;   // second MMA issuer: token columns [BN/2, BN)
+  static constexpr int kThreads = (kIssue2Warp + 1) * 32;
   static constexpr uint32_t kBStageBytes = 2u * BN * kBK * 2;                        // [2][BN][64] bf16
   static constexpr uint32_t kWStageBytes = W4 ? (uint32_t)(kW4SuperInt4Bytes + 512)  // int4 + <= 2 scale groups
                                               : (uint32_t)(2 * kBM * kBK * 2);       // bf16 [2][128][64]
@@ -98,7 +104,8 @@ struct __align__(8) GemmBars {
   uint64_t b_full[16], b_empty[16];
   uint64_t a_full[8], a_empty[8];
   uint64_t acc_full[2], acc_empty[2];
-  uint64_t mma_done;
+  uint64_t mma_done[2];
+  uint32_t ready;              // stages published to the MMA issuer by the waiter warp
   uint32_t tmem_base;
   int abort;
   int total_tiles;
@@ -131,35 +138,6 @@ __device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_
   return ti;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ __nv_bfloat162 bits_bf16x2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
-
-// Dequantise one 16-byte half-row (32 K values, w4_layout.cuh) into the 16 bf16x2 registers
-// of its K pairs in order: pair m = 4i + c lives in word c, slot i.
-__device__ __forceinline__ void dequant_half(const uint4 v, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo,
-                                             const __nv_bfloat162 off136, uint32_t (&o)[16]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t x = ((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16 pair (128 + u)
-      const __nv_bfloat162 q = __hsub2(bits_bf16x2(x), off136);            // exact q = u - 8
-      const __nv_bfloat162 t = __hmul2(q, s_lo);                            // exact (<= 6 bits)
-      o[4 * i + c] = bf16x2_bits(__hfma2(q, s_hi, t));                      // one rounding of q*s
-    }
-  }
-}
-
-// Exact split of an fp16 scale into bf16 hi (top 8 significant bits) + lo (the rest).
-__device__ __forceinline__ void split_scale(uint16_t sbits, __nv_bfloat162& s_hi, __nv_bfloat162& s_lo) {
-  const float sf = __half2float(__ushort_as_half(sbits));
-  const __nv_bfloat16 hi = __float2bfloat16_rz(sf);
-  const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(sf, __bfloat162float(hi)));
-  s_hi = __nv_bfloat162(hi, hi);
-  s_lo = __nv_bfloat162(lo, lo);
-}
-
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4, int BOX>
@@ -182,22 +160,24 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
   if (tid == 0) {
     for (int s = 0; s < WST; ++s) {
       mbar_init(&bars->w_full[s], 1);
-      mbar_init(&bars->w_empty[s], W4 ? 4 : 1);   // W4: the 4 warps of the owning group
+      mbar_init(&bars->w_empty[s], W4 ? 4 : 2);   // W4: the 4 warps of the owning group; bf16: both issuers
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bars->b_full[s], 1);
-      mbar_init(&bars->b_empty[s], 1);
+      mbar_init(&bars->b_empty[s], 2);   // one commit per MMA issuer
     }
     for (int s = 0; s < AST; ++s) {
       mbar_init(&bars->a_full[s], 4);
-      mbar_init(&bars->a_empty[s], 1);
+      mbar_init(&bars->a_empty[s], 2);
     }
     for (int s = 0; s < ACC; ++s) {
-      mbar_init(&bars->acc_full[s], 1);
+      mbar_init(&bars->acc_full[s], 2);
       mbar_init(&bars->acc_empty[s], 128);
     }
-    mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->mma_done[0], 1);
+    mbar_init(&bars->mma_done[1], 1);
     bars->abort = 0;
+    bars->ready = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_x);
@@ -288,33 +268,34 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
       const uint32_t first = it > (uint32_t)WST ? it - WST : 0u;
       for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->w_full[j % WST], (j / WST) & 1u, a.err, nullptr, kSite + 4);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == C::kIssue2Warp) {
+    // ------------------------------------------------------------------ MMA issuers
+    // Two issuing threads, each owning half of the token columns of every tile: an issuing
+    // thread blocks for the duration of each MMA it issues, so while one commits or polls
+    // the other keeps the tensor pipe busy.
+    const int half = warp == 1 ? 0 : 1;
     if (lane == 0) {
       uint32_t it = 0, lt = 0;
       int e_hint = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++lt) {
         const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
-        const uint32_t n_eff = (uint32_t)((ti.rows + 15) & ~15);
-        const uint32_t idesc = idesc_bf16_f32(kBM, n_eff);
+        const int n_eff = (ti.rows + 15) & ~15;
+        int n_mine = n_eff - half * (BN / 2);   // this issuer's columns, a multiple of 16
+        n_mine = n_mine < 0 ? 0 : (n_mine > BN / 2 ? BN / 2 : n_mine);
+        const uint32_t idesc = idesc_bf16_f32(kBM, n_mine > 0 ? (uint32_t)n_mine : 16u);
         const uint32_t acc = lt % ACC;
-        if (!mbar_wait(&bars->acc_empty[acc], ((lt / ACC) & 1u) ^ 1u, a.err, abort_flag, kSite + 5)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * BN;
+        const uint32_t d_tmem = tmem + acc * BN + half * (BN / 2);
         for (int ks = 0; ks < KS; ++ks, ++it) {
           const int sb = it % BST;
           const int sa = it % (W4 ? AST : WST);
-          if (W4) {
-            if (!mbar_wait(&bars->a_full[sa], (it / AST) & 1u, a.err, abort_flag, kSite + 6)) { ok = false; break; }
-          } else {
-            if (!mbar_wait(&bars->w_full[sa], (it / WST) & 1u, a.err, abort_flag, kSite + 6)) { ok = false; break; }
-          }
-          if (!mbar_wait(&bars->b_full[sb], (it / BST) & 1u, a.err, abort_flag, kSite + 7)) { ok = false; break; }
+          // the waiter warp publishes a stage once its operands have landed and, at a tile
+          // start, once the accumulator buffer is free
+          if (!counter_wait(&bars->ready, it, a.err, abort_flag, kSite + 6)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t bsm = smem_u32(b_stages + sb * C::kBStageBytes);
+          const uint32_t bsm = smem_u32(b_stages + sb * C::kBStageBytes) + half * (BN / 2) * kBK * 2;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
+          for (int j = 0; j < 2 && n_mine > 0; ++j) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
               const uint64_t bdesc = sdesc_k_sw128(bsm + j * BN * kBK * 2 + kk * 32);
@@ -332,8 +313,8 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
         }
         if (ok) mma_commit(&bars->acc_full[acc]);
       }
-      mma_commit(&bars->mma_done);
-      mbar_wait(&bars->mma_done, 0, a.err, nullptr, kSite + 8);
+      mma_commit(&bars->mma_done[half]);
+      mbar_wait(&bars->mma_done[half], 0, a.err, nullptr, kSite + 8);
     }
   } else if (W4 && warp < C::kEpiWarp0) {
     // ------------------------------------------------------------------ int4 dequantisers
@@ -379,18 +360,27 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_st16(taddr + c * 16, o[c]);
         } else {
-          // register-limited (many warps): dequantise and store 16 columns at a time
+          // register-limited (many warps): the first k-block is dequantised before the wait
+          // for the TMEM stage, the second 16 columns at a time after it
+          uint32_t o[2][16];
+          {
+            __nv_bfloat162 s_hi, s_lo;
+            split_scale(sb0, s_hi, s_lo);
+            dequant_half(v[0], s_hi, s_lo, off136, o[0]);
+            dequant_half(v[1], s_hi, s_lo, off136, o[1]);
+          }
           if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
+          tmem_st16(taddr, o[0]);
+          tmem_st16(taddr + 16, o[1]);
+          {
             __nv_bfloat162 s_hi, s_lo;
-            split_scale(j == 0 ? sb0 : sb1, s_hi, s_lo);
+            split_scale(sb1, s_hi, s_lo);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              uint32_t o[16];
-              dequant_half(v[2 * j + h], s_hi, s_lo, off136, o);
-              tmem_st16(taddr + (2 * j + h) * 16, o);
+              uint32_t o1[16];
+              dequant_half(v[2 + h], s_hi, s_lo, off136, o1);
+              tmem_st16(taddr + (2 + h) * 16, o1);
             }
           }
         }
@@ -398,6 +388,30 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->a_full[as]);
+      }
+    }
+  } else if (warp == C::kWaitWarp) {
+    // ------------------------------------------------------------------ MMA issuer's waiter
+    // An mbarrier wait in the MMA-issuing thread costs ~270 cycles even when the phase has
+    // long completed (a shared-memory load ~40), so this warp does the issuer's waits and
+    // publishes the count of ready stages.
+    if (lane == 0) {
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++lt) {
+        const uint32_t acc = lt % ACC;
+        if (!mbar_wait(&bars->acc_empty[acc], ((lt / ACC) & 1u) ^ 1u, a.err, abort_flag, kSite + 5)) break;
+        for (int ks = 0; ks < KS; ++ks, ++it) {
+          const int sb = it % BST;
+          const int sa = it % (W4 ? AST : WST);
+          const bool ready = W4 ? mbar_wait(&bars->a_full[sa], (it / AST) & 1u, a.err, abort_flag, kSite + 13)
+                                : mbar_wait(&bars->w_full[sa], (it / WST) & 1u, a.err, abort_flag, kSite + 13);
+          if (!ready || !mbar_wait(&bars->b_full[sb], (it / BST) & 1u, a.err, abort_flag, kSite + 7)) {
+            ok = false;
+            break;
+          }
+          st_release_shared(&bars->ready, it + 1);
+        }
       }
     }
   } else if (warp >= C::kEpiWarp0) {

@@ -97,6 +97,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// A progress counter in shared memory, for threads that must not wait on mbarriers
+// themselves: on B200 an mbarrier wait in a thread that issues tcgen05.mma costs ~270
+// cycles even when the phase has long completed, a plain shared-memory load ~40.  A helper
+// thread waits on the mbarrier (acquire) and publishes the count with a release store; the
+// issuing thread polls it with acquire loads.
+__device__ __forceinline__ uint32_t ld_acquire_shared(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_shared(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+// Bounded wait until *ctr > target (same error / abort contract as mbar_wait).
+__device__ __forceinline__ bool counter_wait(const uint32_t* ctr, uint32_t target, uint32_t* err,
+                                             volatile int* abort, uint32_t site) {
+  if (ld_acquire_shared(ctr) > target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (ld_acquire_shared(ctr) > target) return true;
+    if (((++spins) & 255u) == 0u) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        report_error(err, kErrTimeout, site);
+        if (abort) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // TMA
 // ---------------------------------------------------------------------------------------
