@@ -351,6 +351,117 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Small batches (at most kSmallTokens tokens, i.e. one 128-token tile): the tensor-core
+// kernel above would run on a single SM, streaming the whole batch through one CTA.
+// Instead one warp per (token, expert) computes the logit as a CUDA-core dot product
+// (16-byte loads, fp32 accumulation, fixed butterfly reduction: deterministic), and one CTA
+// routes the tokens with the same arithmetic as the epilogue above and builds the stable
+// (expert, token, slot) permutation.
+// ---------------------------------------------------------------------------------------
+constexpr int kSmallTokens = 128;
+
+__global__ void __launch_bounds__(256) router_small_logits_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const float* __restrict__ bias, int T, int d,
+                                                                   int E, float* __restrict__ logits) {
+  const int t = blockIdx.x;
+  const int e = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T || e >= E) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * d);
+  const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)e * d);
+  float acc = 0.0f;
+  for (int i = lane; i < d / 8; i += 32) {
+    const uint4 xv = xr[i], wv = wr[i];
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xa[j]));
+      const float2 wf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wa[j]));
+      acc = __fmaf_rn(xf.x, wf.x, acc);
+      acc = __fmaf_rn(xf.y, wf.y, acc);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if (lane == 0) logits[(int64_t)t * E + e] = bias ? __fadd_rn(acc, bias[e]) : acc;
+}
+
+template <int KMAX>
+__global__ void __launch_bounds__(kSmallTokens) router_small_route_kernel(const float* __restrict__ logits, int T,
+                                                                           int E, int k, RouterArgs a) {
+  __shared__ int32_t sids[kSmallTokens * 16];
+  __shared__ int32_t scnt[kMaxExperts];
+  __shared__ int32_t snext[kMaxExperts];
+  const int t = threadIdx.x;
+  for (int e = t; e < E; e += blockDim.x) scnt[e] = 0;
+  if (t < T) {
+    // same sequence as the tensor-core path's epilogue: max, sum of exp(l - max),
+    // reciprocal, probabilities into the insertion top-k, reciprocal renormalisation
+    const float* l = logits + (int64_t)t * E;
+    float m = -INFINITY;
+    for (int e = 0; e < E; ++e) m = fmaxf(m, l[e]);
+    float sum = 0.0f;
+    for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, softmax_exp(__fsub_rn(l[e], m)));
+    const float inv = __frcp_rn(sum);
+    float tv[KMAX];
+    int ti[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
+    for (int e = 0; e < E; ++e) topk_insert<KMAX>(tv, ti, __fmul_rn(softmax_exp(__fsub_rn(l[e], m)), inv), e);
+    float ssum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j)
+      if (j < k) ssum = __fadd_rn(ssum, tv[j]);
+    const float invs = __frcp_rn(ssum);
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < k) {
+        const float wj = __fmul_rn(tv[j], invs);
+        a.ids[t * k + j] = ti[j];
+        if (a.weights) a.weights[t * k + j] = wj;
+        if (a.weights_bf16) a.weights_bf16[t * k + j] = __float2bfloat16_rn(wj);
+        sids[t * k + j] = ti[j];
+      }
+    }
+  }
+  if (!a.do_perm) return;
+  __syncthreads();
+  const int n = T * k;
+  for (int f = t; f < n; f += blockDim.x) atomicAdd(&scnt[sids[f]], 1);
+  __syncthreads();
+  if (t == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      a.counts[e] = scnt[e];
+      a.offsets[e] = run;
+      snext[e] = run;
+      run += scnt[e];
+    }
+    a.offsets[E] = run;
+  }
+  __syncthreads();
+  // warp 0 walks the flat indices in order, 32 at a time: equal experts in a chunk take
+  // consecutive slots in lane order, so the result is ordered by (expert, token, slot)
+  if (t < 32) {
+    for (int c = 0; c < n; c += 32) {
+      const int f = c + t;
+      const int e = f < n ? sids[f] : E;
+      const uint32_t peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << t) - 1u));
+      const int base = e < E ? snext[e] : 0;
+      __syncwarp();
+      if (f < n) {
+        a.sorted_idx[base + rank] = f;
+        if (a.positions) a.positions[f] = base + rank;
+        if (rank == 0) snext[e] = base + __popc(peers);
+      }
+      __syncwarp();
+    }
+  }
+}
+
 template <int KMAX>
 int launch_router(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const RouterArgs& a, int grid, size_t smem,
                   cudaStream_t stream) {
@@ -416,7 +527,9 @@ extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_expert
   bytes += (size_t)tiles * num_experts * sizeof(int32_t);
   bytes = (bytes + 255) & ~size_t(255);
   bytes += (size_t)tiles * num_experts * 4 * sizeof(uint32_t);
-  return bytes;
+  // small batches keep the fp32 logits after the 256-byte header
+  const size_t small = num_tokens <= kSmallTokens ? 256 + (((size_t)num_tokens * num_experts * 4 + 255) & ~size_t(255)) : 0;
+  return bytes > small ? bytes : small;
 }
 
 extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
@@ -452,6 +565,30 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   if (dev.cc_major != 10) return LMOE_ERR_DEVICE;
 
   const int E = num_experts;
+  if (num_tokens <= kSmallTokens) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    LMOE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, stream));
+    float* lg = logits ? logits : reinterpret_cast<float*>(ws + 256);
+    RouterArgs a = {};
+    a.ids = ids;
+    a.weights = weights;
+    a.weights_bf16 = static_cast<__nv_bfloat16*>(weights_bf16);
+    a.counts = counts;
+    a.offsets = offsets;
+    a.sorted_idx = sorted_idx;
+    a.positions = do_perm ? positions : nullptr;
+    a.do_perm = do_perm ? 1 : 0;
+    const int T = (int)num_tokens;
+    router_small_logits_kernel<<<dim3(T, (E + 7) / 8), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(gate_weight), gate_bias, T,
+        hidden_size, E, lg);
+    LMOE_CUDA_TRY(cudaGetLastError());
+    if (top_k <= 2) router_small_route_kernel<2><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
+    else if (top_k <= 4) router_small_route_kernel<4><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
+    else if (top_k <= 8) router_small_route_kernel<8><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
+    else router_small_route_kernel<16><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
+    return cuda_status(cudaGetLastError());
+  }
   const int Epad = ((E + 15) / 16) * 16;
   const int num_tiles = (int)((num_tokens + kBM - 1) / kBM);
   const uint32_t stage_bytes = kBM * kBK * 2 + Epad * kBK * 2;
