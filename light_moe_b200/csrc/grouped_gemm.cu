@@ -22,15 +22,15 @@
 // and both operands are read from shared memory ("SS" form).
 //
 // Warp roles (one CTA per SM, persistent over a static round-robin tile schedule):
-//   warp 0            token-tile producer (TMA)
+//   warp 0            producer: token tiles (TMA) and weights (bulk copy of int4 super-blocks
+//                     / TMA of bf16 tiles), the weights up to WST - BST stages ahead
 //   warp 1            MMA issuer (one thread) for token columns [0, BN/2) of every tile
-//   warp 2            weight producer (bulk copy of int4 super-blocks / TMA of bf16 tiles)
+//   warp 2            MMA issuer for token columns [BN/2, BN)
 //   warps 3..3+DQ-1   int4 dequantisers (W4 only), DQ/4 groups of 4 warps; a group owns
 //                     every (DQ/4)-th stage, one weight row per thread
 //   next 4 warps      epilogue: TMEM -> registers -> (SwiGLU | scale+scatter) -> global
-//   next warp         the MMA issuers' waiter: waits on the stage and accumulator barriers
+//   last warp         the MMA issuers' waiter: waits on the stage and accumulator barriers
 //                     and publishes a counter the issuers poll
-//   last warp         second MMA issuer, token columns [BN/2, BN)
 // Every stage covers 128 K values (two 64-wide swizzle atoms), so each mbarrier wait,
 // expect-tx and commit is amortised over eight 128 x N x 16 MMAs, and the two producers
 // issue their copies in parallel.
@@ -75,14 +75,17 @@ struct GemmArgs {
   uint32_t tmem_cols;
 };
 
+constexpr int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
+constexpr int lcm_int(int a, int b) { return a / gcd_int(a, b) * b; }
+
 template <int BN, int DQ, int WST, int BST, int AST, int ACC, bool W4, int BOX>
 struct Cfg {
   static constexpr int kDQWarps = W4 ? DQ : 0;
   static constexpr int kGroups = W4 ? DQ / 4 : 1;
   static constexpr int kEpiWarp0 = 3 + kDQWarps;
   static constexpr int kWaitWarp = kEpiWarp0 + 4;
-  static constexpr int kIssue2Warp = kWaitWarp + 1;   // second MMA issuer: token columns [BN/2, BN)
-  static constexpr int kThreads = (kIssue2Warp + 1) * 32;
+  static constexpr int kIssue2Warp = 2;   // second MMA issuer: token columns [BN/2, BN)
+  static constexpr int kThreads = (kWaitWarp + 1) * 32;
   static constexpr uint32_t kBStageBytes = 2u * BN * kBK * 2;                        // [2][BN][64] bf16
   static constexpr uint32_t kWStageBytes = W4 ? (uint32_t)(kW4SuperInt4Bytes + 512)  // int4 + <= 2 scale groups
                                               : (uint32_t)(2 * kBM * kBK * 2);       // bf16 [2][128][64]
@@ -92,6 +95,11 @@ struct Cfg {
   // dequantise a whole stage into registers before waiting for its TMEM stage when the
   // register file allows it (65536 registers / threads >= ~128)
   static constexpr bool kEarlyDequant = kThreads <= 512;
+  // "stage done" ring: one barrier per stage modulo kRing, a multiple of the A (W4) or weight
+  // (bf16) ring and of the token ring, so one commit per issuer and stage frees both slots
+  static constexpr int kAR = W4 ? AST : WST;
+  static constexpr int kRing = lcm_int(kAR, BST);
+  static_assert(kRing <= 16, "stage-done ring");
   static_assert(BN % BOX == 0 && BOX % 8 == 0 && BN % 16 == 0, "token tile = whole boxes of whole swizzle atoms");
   static_assert(!W4 || DQ % 4 == 0, "dequantiser groups of four warps");
   // A stage ring may only be waited on by one group: an mbarrier parity wait is exact only
@@ -101,8 +109,9 @@ struct Cfg {
 
 struct __align__(8) GemmBars {
   uint64_t w_full[16], w_empty[16];
-  uint64_t b_full[16], b_empty[16];
-  uint64_t a_full[8], a_empty[8];
+  uint64_t b_full[16];
+  uint64_t a_full[8];
+  uint64_t stage_done[16];     // both issuers' MMAs of stage it finished (index it % kRing)
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done[2];
   uint32_t ready;              // stages published to the MMA issuer by the waiter warp
@@ -160,20 +169,21 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
   if (tid == 0) {
     for (int s = 0; s < WST; ++s) {
       mbar_init(&bars->w_full[s], 1);
-      mbar_init(&bars->w_empty[s], W4 ? 4 : 2);   // W4: the 4 warps of the owning group; bf16: both issuers
+      mbar_init(&bars->w_empty[s], 4);   // W4: the 4 warps of the owning dequantiser group
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bars->b_full[s], 1);
-      mbar_init(&bars->b_empty[s], 2);   // one commit per MMA issuer
+
     }
     for (int s = 0; s < AST; ++s) {
       mbar_init(&bars->a_full[s], 4);
-      mbar_init(&bars->a_empty[s], 2);
+
     }
     for (int s = 0; s < ACC; ++s) {
       mbar_init(&bars->acc_full[s], 2);
       mbar_init(&bars->acc_empty[s], 128);
     }
+    for (int s = 0; s < C::kRing; ++s) mbar_init(&bars->stage_done[s], 2);   // one commit per MMA issuer
     mbar_init(&bars->mma_done[0], 1);
     mbar_init(&bars->mma_done[1], 1);
     bars->abort = 0;
@@ -181,7 +191,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_x);
-  if (!W4 && warp == 2 && lane == 0) tma_prefetch_desc(&tm_w);
+  if (!W4 && warp == 0 && lane == 0) tma_prefetch_desc(&tm_w);
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, a.tmem_cols);
     tmem_relinquish();
@@ -216,18 +226,55 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
   const int KS = a.KS;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ token-tile producer
+    // ------------------------------------------------------------------ producer
+    // One thread issues both streams: the weight copies (one bulk copy of an int4
+    // super-block, or two TMA boxes of bf16) run up to kWLead stages ahead of the token
+    // tiles, which have the shorter ring.
     if (lane == 0) {
-      uint32_t it = 0;
-      int e_hint = 0;
+      constexpr int kWLead = WST > BST ? WST - BST : 0;
+      uint32_t it = 0, it_w = 0;
+      int e_hint = 0, w_hint = 0, tile_w = blockIdx.x, ks_w = 0;
+      TileInfo ti_w = {};
+      if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint);
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
         const int nbox = (ti.rows + BOX - 1) / BOX;   // only the boxes that cover this tile's rows
         const uint32_t bytes = (uint32_t)(2 * nbox * BOX * kBK * 2);
         for (int ks = 0; ks < KS; ++ks, ++it) {
+          // weights of stages up to it + kWLead
+          while (tile_w < total && it_w <= it + kWLead) {
+            const int s = it_w % WST;
+            const bool w_free =
+                W4 ? mbar_wait(&bars->w_empty[s], ((it_w / WST) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)
+                   : (it_w < (uint32_t)WST ||
+                      mbar_wait(&bars->stage_done[(it_w - WST) % C::kRing], ((it_w - WST) / C::kRing) & 1u, a.err,
+                                abort_flag, kSite + 3));
+            if (!w_free) { ok = false; break; }
+            uint8_t* wsm = w_stages + s * C::kWStageBytes;
+            if (W4) {
+              const uint8_t* wblk = a.wq + (size_t)(ti_w.w * a.NB + ti_w.fb) * KS * a.sb_bytes;
+              mbar_arrive_expect_tx(&bars->w_full[s], a.sb_bytes);
+              bulk_load(wsm, wblk + (size_t)ks_w * a.sb_bytes, a.sb_bytes, &bars->w_full[s]);
+            } else {
+              mbar_arrive_expect_tx(&bars->w_full[s], 2 * kBM * kBK * 2);
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                tma_load_2d(wsm + j * kBM * kBK * 2, &tm_w, &bars->w_full[s], (2 * ks_w + j) * kBK,
+                            ti_w.w * a.N + ti_w.fb * kBM);
+            }
+            ++it_w;
+            if (++ks_w == KS) {
+              ks_w = 0;
+              tile_w += gridDim.x;
+              if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint);
+            }
+          }
+          if (!ok) break;
           const int s = it % BST;
-          if (!mbar_wait(&bars->b_empty[s], ((it / BST) & 1u) ^ 1u, a.err, abort_flag, kSite + 1)) { ok = false; break; }
+          if (it >= (uint32_t)BST &&
+              !mbar_wait(&bars->stage_done[(it - BST) % C::kRing], ((it - BST) / C::kRing) & 1u, a.err, abort_flag,
+                         kSite + 1)) { ok = false; break; }
           uint8_t* bsm = b_stages + s * C::kBStageBytes;
           mbar_arrive_expect_tx(&bars->b_full[s], bytes);
 #pragma unroll
@@ -237,36 +284,11 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
                           ti.row0 + bx * BOX);
         }
       }
-      const uint32_t first = it > (uint32_t)BST ? it - BST : 0u;   // drain copies in flight
+      // no copy of this CTA may still be in flight when it exits
+      const uint32_t first = it > (uint32_t)BST ? it - BST : 0u;
       for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->b_full[j % BST], (j / BST) & 1u, a.err, nullptr, kSite + 2);
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ weight producer
-    if (lane == 0) {
-      uint32_t it = 0;
-      int e_hint = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
-        const uint8_t* wblk = W4 ? a.wq + (size_t)(ti.w * a.NB + ti.fb) * KS * a.sb_bytes : nullptr;
-        for (int ks = 0; ks < KS; ++ks, ++it) {
-          const int s = it % WST;
-          if (!mbar_wait(&bars->w_empty[s], ((it / WST) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)) { ok = false; break; }
-          uint8_t* wsm = w_stages + s * C::kWStageBytes;
-          if (W4) {
-            mbar_arrive_expect_tx(&bars->w_full[s], a.sb_bytes);
-            bulk_load(wsm, wblk + (size_t)ks * a.sb_bytes, a.sb_bytes, &bars->w_full[s]);
-          } else {
-            mbar_arrive_expect_tx(&bars->w_full[s], 2 * kBM * kBK * 2);
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-              tma_load_2d(wsm + j * kBM * kBK * 2, &tm_w, &bars->w_full[s], (2 * ks + j) * kBK,
-                          ti.w * a.N + ti.fb * kBM);
-          }
-        }
-      }
-      const uint32_t first = it > (uint32_t)WST ? it - WST : 0u;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->w_full[j % WST], (j / WST) & 1u, a.err, nullptr, kSite + 4);
+      const uint32_t first_w = it_w > (uint32_t)WST ? it_w - WST : 0u;
+      for (uint32_t j = first_w; j < it_w; ++j) mbar_wait(&bars->w_full[j % WST], (j / WST) & 1u, a.err, nullptr, kSite + 4);
     }
   } else if (warp == 1 || warp == C::kIssue2Warp) {
     // ------------------------------------------------------------------ MMA issuers
@@ -308,8 +330,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
               }
             }
           }
-          mma_commit(W4 ? &bars->a_empty[sa] : &bars->w_empty[sa]);
-          mma_commit(&bars->b_empty[sb]);
+          mma_commit(&bars->stage_done[it % C::kRing]);   // frees the A / weight and token slots
         }
         if (ok) mma_commit(&bars->acc_full[acc]);
       }
@@ -355,7 +376,9 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
               dequant_half(v[2 * j + h], s_hi, s_lo, off136, o[2 * j + h]);
             }
           }
-          if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
+          if (it >= (uint32_t)AST &&
+              !mbar_wait(&bars->stage_done[(it - AST) % C::kRing], ((it - AST) / C::kRing) & 1u, a.err, abort_flag,
+                         kSite + 11)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_st16(taddr + c * 16, o[c]);
@@ -369,7 +392,9 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
             dequant_half(v[0], s_hi, s_lo, off136, o[0]);
             dequant_half(v[1], s_hi, s_lo, off136, o[1]);
           }
-          if (!mbar_wait(&bars->a_empty[as], ((it / AST) & 1u) ^ 1u, a.err, abort_flag, kSite + 11)) { ok = false; break; }
+          if (it >= (uint32_t)AST &&
+              !mbar_wait(&bars->stage_done[(it - AST) % C::kRing], ((it - AST) / C::kRing) & 1u, a.err, abort_flag,
+                         kSite + 11)) { ok = false; break; }
           tc_fence_after();
           tmem_st16(taddr, o[0]);
           tmem_st16(taddr + 16, o[1]);
