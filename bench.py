@@ -291,7 +291,7 @@ def run_ours(args):
                       "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4),
                       "roofline_gate_up": droof}
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and ws == 1:   # the CPU baseline is a single-GPU (rank 0, N=1) figure
             v, cores, sample = cpu_baseline(ex, gw, args.cpu_tokens)
             cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
         result = {

@@ -41,8 +41,11 @@ def _logit_bound(x, w):
     return (ax @ aw.T) * 2.0 ** -18 + 1e-30
 
 
+# T <= 128 runs the small-batch path (warp dot products + one routing CTA), larger T the
+# tensor-core kernel; (128, ...) and (129, ...) sit on either side of the switch
 @pytest.mark.parametrize("T,d,E,k", [(1, 64, 8, 2), (64, 4096, 8, 2), (257, 128, 16, 4), (300, 256, 64, 6),
-                                     (1000, 512, 8, 1), (129, 64, 256, 16), (77, 192, 40, 7), (512, 1024, 64, 8)])
+                                     (1000, 512, 8, 1), (129, 64, 256, 16), (77, 192, 40, 7), (512, 1024, 64, 8),
+                                     (128, 256, 256, 16), (128, 128, 8, 2)])
 def test_router_bitexact_given_logits(T, d, E, k):
     x, w = _inputs(T, d, E, seed=T + E)
     out = router(x, w, k)
@@ -52,7 +55,8 @@ def test_router_bitexact_given_logits(T, d, E, k):
     assert out["ids"].min() >= 0 and out["ids"].max() < E
 
 
-@pytest.mark.parametrize("T,d,E,k", [(257, 128, 16, 4), (512, 4096, 64, 6), (1024, 2048, 8, 2)])
+@pytest.mark.parametrize("T,d,E,k", [(257, 128, 16, 4), (512, 4096, 64, 6), (1024, 2048, 8, 2), (64, 4096, 8, 2),
+                                     (100, 512, 64, 6)])
 def test_router_logits_and_end_to_end_ids(T, d, E, k):
     x, w = _inputs(T, d, E, seed=7 * T + E)
     out = router(x, w, k)
@@ -98,6 +102,16 @@ def test_router_ties_go_to_lower_expert_id():
     x0 = torch.zeros(4, d, dtype=torch.bfloat16, device="cuda")
     out0 = router(x0, w, k)
     assert out0["ids"].tolist() == [[0, 1, 2]] * 4
+
+
+@pytest.mark.parametrize("T,d,E,k", [(64, 1024, 8, 2), (300, 256, 16, 4)])
+def test_router_positions_invert_the_permutation(T, d, E, k):
+    x, w = _inputs(T, d, E, seed=19 + T)
+    out = router(x, w, k, positions=True)
+    _check_given_logits(out, k, E)
+    sidx, pos = out["sorted_idx"], out["positions"]
+    assert np.array_equal(np.sort(sidx), np.arange(T * k))
+    assert np.array_equal(pos[sidx], np.arange(T * k))
 
 
 def test_router_bias():
