@@ -235,9 +235,9 @@ def run_ours(args):
     x, gw, ex = make_problem(T, device, seed=0)
     if ws > 1:
         from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
-        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None)
+        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, micro_batches=args.micro_batches)
         fwd = layer.forward
-        launches_per_step = layer.kernels_per_step
+        launches_per_step = 5 * layer.micro_batches
     else:
         layer = W4A16MoELayer(gw, ex, TOPK)
         fwd = layer.forward
@@ -303,6 +303,7 @@ def run_ours(args):
             "config": {"workload": "Mixtral-8x7B-shaped W4A16 MoE layer, prefill", "tokens_per_gpu": T,
                        "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP,
                        "parallelism": f"ep{ws}" if ws > 1 else "single GPU",
+                       "ep_micro_batches": args.micro_batches if ws > 1 else None,
                        "l2": "inputs larger than L2 (727 MB int4 weights streamed every step)"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                     "d2h_bytes_per_step": T * D * 2},
@@ -370,6 +371,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--cpu-tokens", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro-batches", type=int, default=1,
+                    help="expert-parallel runs: micro-batches whose all-to-alls overlap the GEMMs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

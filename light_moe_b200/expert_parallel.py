@@ -20,6 +20,14 @@ to equal splits and applies local expert 0 to every token, with the real computa
   7. weighted combine into the token order with the inverse permutation (fp32, slot order);
      always-on shared experts run locally on the rank's tokens in the same GEMM launches.
 
+With ``micro_batches`` > 1 (the same value on every rank: it fixes the sequence of
+collectives) each rank's tokens are split into that many contiguous micro-batches, possibly
+empty: all of them are routed and gathered first and their counts travel in one
+all-to-all (one host synchronisation per forward); then the dispatch all-to-alls are
+enqueued back to back on NCCL's stream while the GEMMs of micro-batch m run on the compute
+stream, and the combine all-to-all of m overlaps the GEMMs of m + 1.  Each token's
+arithmetic is unchanged.
+
 The steps that move data between ranks use ``torch.distributed`` collectives, so the
 whole flow also runs with the gloo backend on CPU processes when a CPU expert backend is
 supplied (the tests do this); the product backend is the CUDA library.
@@ -91,6 +99,12 @@ class ExpertParallelGroup:
         dist.all_to_all_single(output_tensor, input_tensor, output_split_sizes, input_split_sizes, group=self.group)
         return output_tensor
 
+    def all_to_all_async(self, output_tensor, input_tensor, output_split_sizes=None, input_split_sizes=None):
+        """Enqueue an all-to-all-v and return its work handle; ``wait()`` on it orders the
+        caller's current CUDA stream after the transfer without blocking the host."""
+        return dist.all_to_all_single(output_tensor, input_tensor, output_split_sizes, input_split_sizes,
+                                      group=self.group, async_op=True)
+
     def all_reduce(self, tensor):
         dist.all_reduce(tensor, group=self.group)
         return tensor
@@ -131,7 +145,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
     """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks."""
 
     def __init__(self, config: ExpertParallelConfig, ep_group: ExpertParallelGroup, gate_weight: torch.Tensor,
-                 backend, gate_bias: Optional[torch.Tensor] = None):
+                 backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1):
         super().__init__()
         self.config = config
         self.ep_group = ep_group
@@ -141,13 +155,16 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         self.experts_per_rank = config.experts_per_rank
         self.local_expert_start = ep_group.rank * self.experts_per_rank
         self.local_expert_end = self.local_expert_start + self.experts_per_rank
-        # kernels of ours per forward: router, gather, gate/up GEMM, down GEMM, combine
+        self.micro_batches = max(1, int(micro_batches))   # must be equal on all ranks
+        # kernels of ours per forward: router, gather, gate/up GEMM, down GEMM, combine per
+        # micro-batch (set by the last forward)
         self.kernels_per_step = 5
         self._seg_cache = {}
 
     @classmethod
     def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
-                  group: Optional[dist.ProcessGroup] = None, gate_bias: Optional[torch.Tensor] = None):
+                  group: Optional[dist.ProcessGroup] = None, gate_bias: Optional[torch.Tensor] = None,
+                  micro_batches: int = 1):
         """Build this rank's layer from the full (all-expert) prepacked weights."""
         ws = dist.get_world_size(group)
         g = ExpertParallelGroup(ws).attach(group)
@@ -155,7 +172,8 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
                                    intermediate_size=experts.ffn_size, ep_size=ws, group_size=experts.group_size,
                                    num_shared=experts.num_shared)
         local = slice_experts(experts, g.rank * cfg.experts_per_rank, (g.rank + 1) * cfg.experts_per_rank)
-        return cls(cfg, g, gate_weight.to(torch.bfloat16).contiguous(), CudaExpertBackend(local, top_k), gate_bias)
+        return cls(cfg, g, gate_weight.to(torch.bfloat16).contiguous(), CudaExpertBackend(local, top_k), gate_bias,
+                   micro_batches)
 
     def _segments(self, device):
         key = (str(device),)
@@ -171,36 +189,61 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         cfg, g, be = self.config, self.ep_group, self.backend
         ep, epr, k, S = g.ep_size, self.experts_per_rank, cfg.top_k, cfg.num_shared
         dev = x.device
+        nmb = self.micro_batches
+        bounds = [(T * m // nmb, T * (m + 1) // nmb) for m in range(nmb)]
+        self.kernels_per_step = 5 * nmb
 
-        ids, w, counts, offsets, sidx, pos = be.route(x, self.gate_weight, self.gate_bias)
-        rows = be.gather(x, sidx)                                    # [T*k, d], destination-rank order
+        # 1-2. route and gather every micro-batch (destination-rank order)
+        mbs = []
+        for a, b in bounds:
+            xm = x[a:b]
+            ids, w, counts, offsets, sidx, pos = be.route(xm, self.gate_weight, self.gate_bias)
+            mbs.append({"x": xm, "T": b - a, "w": w, "pos": pos, "counts": counts, "rows": be.gather(xm, sidx)})
 
-        send_counts = counts.view(ep, epr).contiguous()
+        # 3. one count exchange for all micro-batches: send[r, m, e] = rows of micro-batch m
+        #    for expert e of rank r; recv[s, m, e] = rows rank s sends us; one host copy
+        send_counts = torch.stack([mb["counts"].view(ep, epr) for mb in mbs], 1).contiguous()
         recv_counts = torch.empty_like(send_counts)
-        g.all_to_all(recv_counts, send_counts)                       # recv[s, e]: rows from s for expert e
+        g.all_to_all(recv_counts, send_counts)
         both = torch.cat([send_counts.flatten(), recv_counts.flatten()]).cpu()
-        send_splits = both[: ep * epr].view(ep, epr).sum(1).tolist()
-        recv_h = both[ep * epr:].view(ep, epr)
-        recv_splits = recv_h.sum(1).tolist()
-        R = int(sum(recv_splits))
+        send_h = both[: ep * nmb * epr].view(ep, nmb, epr)
+        recv_h = both[ep * nmb * epr:].view(ep, nmb, epr)
 
-        recv = torch.empty(R + S * T, d, dtype=x.dtype, device=dev)
-        g.all_to_all(recv[:R], rows, recv_splits, send_splits)
-        for s in range(S):                                           # shared experts: local tokens
-            recv[R + s * T: R + (s + 1) * T].copy_(x)
+        # 4. dispatch all micro-batches; NCCL runs them in order on its own stream
+        for m, mb in enumerate(mbs):
+            mb["send_splits"] = send_h[:, m].sum(1).tolist()
+            mb["recv_h"] = recv_h[:, m]
+            mb["recv_splits"] = mb["recv_h"].sum(1).tolist()
+            R = int(sum(mb["recv_splits"]))
+            mb["R"] = R
+            mb["recv"] = torch.empty(R + S * mb["T"], d, dtype=x.dtype, device=dev)
+            mb["work"] = g.all_to_all_async(mb["recv"][:R], mb["rows"], mb["recv_splits"], mb["send_splits"])
 
-        seg_counts = recv_h.flatten().tolist() + [T] * S
-        offs = [0]
-        for c in seg_counts:
-            offs.append(offs[-1] + int(c))
-        seg_offsets = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
-        max_rows = max(seg_counts) if seg_counts else 0
-        out = be.experts(recv, seg_offsets, self._segments(dev), len(seg_counts), max_rows)
+        # 5-6. GEMMs of micro-batch m once its rows are here; its combine all-to-all then
+        #      overlaps the GEMMs of the next micro-batch
+        for mb in mbs:
+            mb["work"].wait()
+            R, Tm, recv = mb["R"], mb["T"], mb["recv"]
+            for s in range(S):                                       # shared experts: local tokens
+                recv[R + s * Tm: R + (s + 1) * Tm].copy_(mb["x"])
+            seg_counts = mb["recv_h"].flatten().tolist() + [Tm] * S
+            offs = [0]
+            for c in seg_counts:
+                offs.append(offs[-1] + int(c))
+            seg_offsets = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
+            max_rows = max(seg_counts) if seg_counts else 0
+            out = be.experts(recv, seg_offsets, self._segments(dev), len(seg_counts), max_rows)
+            mb["out"] = out
+            mb["ret"] = torch.empty(Tm * k, d, dtype=x.dtype, device=dev)
+            mb["work"] = g.all_to_all_async(mb["ret"], out[:R].contiguous(), mb["send_splits"], mb["recv_splits"])
 
-        ret = torch.empty(T * k, d, dtype=x.dtype, device=dev)
-        g.all_to_all(ret, out[:R].contiguous(), send_splits, recv_splits)
-        extra = out[R:] if S else None
-        y = be.combine(ret, pos, w, T, extra, S)
+        # 7. weighted combine of each micro-batch
+        ys = []
+        for mb in mbs:
+            mb["work"].wait()
+            extra = mb["out"][mb["R"]:] if S else None
+            ys.append(be.combine(mb["ret"], mb["pos"], mb["w"], mb["T"], extra, S))
+        y = ys[0] if nmb == 1 else torch.cat(ys)
         return y.view(hidden_states.shape)
 
 

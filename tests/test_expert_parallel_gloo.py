@@ -58,7 +58,7 @@ def _worker(rank, world, port, case, q):
         grp = ExpertParallelGroup(world).attach()
         cfg = ExpertParallelConfig(num_experts=E, top_k=k, hidden_size=d, intermediate_size=F, ep_size=world,
                                    group_size=g, num_shared=S)
-        layer = ExpertParallelW4A16Layer(cfg, grp, torch.from_numpy(gw), be)
+        layer = ExpertParallelW4A16Layer(cfg, grp, torch.from_numpy(gw), be, micro_batches=case.get("mb", 1))
         x = np.random.default_rng(100 + rank).standard_normal((Ts[rank], d), dtype=np.float32)
         if case.get("die") is not None and rank == case["die"]:
             be.route(torch.from_numpy(x), torch.from_numpy(gw), None)
@@ -97,6 +97,9 @@ def _run(world, case, timeout=120):
     (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[5, 17])),
     (4, dict(E=8, S=0, k=3, d=64, F=64, g=64, T=[30, 1, 12, 25])),
     (2, dict(E=4, S=2, k=2, d=128, F=64, g=64, T=[3, 64])),
+    # micro-batched dispatch / combine; rank 1 has fewer tokens than micro-batches
+    (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[40, 1], mb=2)),
+    (4, dict(E=8, S=0, k=3, d=64, F=64, g=64, T=[30, 2, 12, 25], mb=3)),
 ])
 def test_expert_parallel_matches_single_process(world, case):
     results, codes = _run(world, case)

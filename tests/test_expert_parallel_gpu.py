@@ -40,7 +40,7 @@ def _worker(rank, world, port, case, q):
         shared = [(w1[E + s], w3[E + s], w2[E + s]) for s in range(S)] or None
         ex = W4A16Experts.from_dense(w1[:E], w3[:E], w2[:E], g, shared=shared)
         bias = torch.linspace(-1, 1, E, device=dev) if case.get("bias") else None
-        ep_layer = ExpertParallelW4A16Layer.from_full(gw, ex, k, gate_bias=bias)
+        ep_layer = ExpertParallelW4A16Layer.from_full(gw, ex, k, gate_bias=bias, micro_batches=case.get("mb", 1))
         ref_layer = W4A16MoELayer(gw, ex, k, gate_bias=bias)
         T = case["T"][rank]
         x = torch.randn(T, d, generator=torch.Generator(device="cpu").manual_seed(10 + rank)).to(torch.bfloat16).to(dev)
@@ -77,7 +77,10 @@ def _run(world, case, timeout=300):
 
 CASES = [dict(E=8, S=0, k=2, d=512, F=256, g=128, T=[300, 77]),
          dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[64, 200], bias=True),
-         dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64])]
+         dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64]),
+         # micro-batched dispatch / combine (one rank with an empty micro-batch)
+         dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[2000, 1], mb=2),
+         dict(E=16, S=0, k=4, d=256, F=128, g=64, T=[333, 150], mb=3)]
 
 
 @pytest.mark.parametrize("case", CASES)
