@@ -178,6 +178,71 @@ def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
             "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
 
 
+# ----------------------------------------------------------------------------- other workloads
+def extra_workloads(ex, stream, peaks, peak_kind, device):
+    """Single-GPU measurements of the other workloads of the hot path (reported beside the
+    headline, never folded into it): the router alone, the Mixtral grouped GEMMs with a
+    skewed expert load, and the fine-grained 64-expert layer."""
+    import torch
+
+    from light_moe_b200 import ops
+    from light_moe_b200.layer import W4A16Experts, W4A16MoELayer
+
+    out = {}
+    g = torch.Generator(device=device).manual_seed(0)
+    # router: x [16384, 4096] bf16, W [E, 4096]; HBM-bound on the x stream
+    T = 16384
+    x = torch.randn(T, D, generator=g, device=device).to(torch.bfloat16)
+    router = []
+    for e, k in ((8, 2), (64, 6)):
+        w = (torch.randn(e, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        secs = time_device(lambda: ops.fused_gate_topk_ex(x, w, k), 20, 3, stream) / 20
+        nbytes = T * D * 2 + e * D * 2 + T * k * 8 + (2 * e + 1) * 4
+        gbs = nbytes / secs / 1e9
+        router.append({"experts": e, "top_k": k, "tokens": T, "us": round(secs * 1e6, 1), "GB/s": round(gbs, 1),
+                       "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes": nbytes})
+    out["router"] = router
+    del x
+    # grouped GEMMs (gate/up + SwiGLU, down) over 8192 rows, Zipf(1.2) expert load
+    R = 8192
+    p = [(i + 1) ** -1.2 for i in range(E)]
+    cnt = [int(R * v / sum(p)) for v in p]
+    cnt[0] += R - sum(cnt)
+    offs = torch.tensor([0] + [sum(cnt[:i + 1]) for i in range(E)], dtype=torch.int32, device=device)
+    xr = torch.randn(R, D, generator=g, device=device).to(torch.bfloat16)
+
+    def gemms():
+        h = ops.w4a16_grouped_gemm(xr, ex.w13_packed, offs, E, 2 * FFN, GROUP, 1, None, None, 0, max(cnt))
+        return ops.w4a16_grouped_gemm(h, ex.w2_packed, offs, E, D, GROUP, 0, None, None, 0, max(cnt))
+
+    secs = time_device(gemms, 10, 3, stream) / 10
+    flops = 2.0 * R * 3 * D * FFN
+    out["grouped_gemm_zipf"] = {"rows": R, "rows_per_expert": cnt, "ms": round(secs * 1e3, 4),
+                                "TFLOP/s": round(flops / secs / 1e12, 1),
+                                "frac_of_bf16_peak": round(flops / secs / 1e12 / peaks["bf16_tflops"], 4)}
+    del xr
+    # fine-grained layer: d=2048, 64 routed experts (ffn 1408) top-6 + 2 shared, int4 g=64
+    d5, f5, e5, k5, s5, g5, t5 = 2048, 1408, 64, 6, 2, 64, 16384
+    w1 = (torch.randn(e5 + s5, f5, d5, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn(e5 + s5, f5, d5, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(e5 + s5, d5, f5, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    shared = [(w1[e5 + i], w3[e5 + i], w2[e5 + i]) for i in range(s5)]
+    ex5 = W4A16Experts.from_dense(w1[:e5], w3[:e5], w2[:e5], g5, shared=shared)
+    del w1, w3, w2
+    gw5 = (torch.randn(e5, d5, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    bias5 = torch.linspace(0.5, -0.5, e5, device=device)   # skews the load toward low ids
+    layer5 = W4A16MoELayer(gw5, ex5, k5, gate_bias=bias5)
+    x5 = torch.randn(t5, d5, generator=g, device=device).to(torch.bfloat16)
+    secs = time_device(lambda: layer5(x5), 10, 3, stream) / 10
+    flops = 2.0 * t5 * (k5 + s5) * 3 * d5 * f5
+    out["fine_grained_layer"] = {"tokens": t5, "hidden": d5, "ffn": f5, "experts": e5, "top_k": k5, "shared": s5,
+                                 "group_size": g5, "ms": round(secs * 1e3, 4), "tokens/s": round(t5 / secs, 1),
+                                 "TFLOP/s": round(flops / secs / 1e12, 1),
+                                 "frac_of_bf16_peak": round(flops / secs / 1e12 / peaks["bf16_tflops"], 4)}
+    out["peak_source"] = peak_kind
+    return out
+
+
 # ----------------------------------------------------------------------------- CPU oracle baseline
 def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
     """The oracle's numpy restatement of SparseMoEBlock on the dequantised weights."""
@@ -290,6 +355,12 @@ def run_ours(args):
                       "layer_weight_stream_gbs": round(layer_gbs, 1),
                       "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4),
                       "roofline_gate_up": droof}
+        extra = None
+        if ws == 1 and not args.no_extra:
+            try:
+                extra = extra_workloads(ex, stream, peaks, peak_kind, device)
+            except Exception as exc:   # reported, never hides the headline line
+                extra = {"error": f"{type(exc).__name__}: {exc}"}
         cpu = None
         if not args.no_cpu_baseline and ws == 1:   # the CPU baseline is a single-GPU (rank 0, N=1) figure
             v, cores, sample = cpu_baseline(ex, gw, args.cpu_tokens)
@@ -310,6 +381,7 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roof,
             "decode": decode,
+            "other_workloads": extra,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -371,6 +443,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--cpu-tokens", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the router / skewed-GEMM / fine-grained measurements")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="expert-parallel runs: micro-batches whose all-to-alls overlap the GEMMs")
     args = ap.parse_args()
