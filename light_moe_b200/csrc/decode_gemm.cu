@@ -504,7 +504,10 @@ int run_decode_gemm(const DecodeProblem& p, cudaStream_t stream) {
   st = encode_tmap_2d(&tm_x32, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,
                       (uint64_t)p.ldx * 2, 32, 64, true);
   if (st != LMOE_OK) return st;
-  LMOE_CUDA_TRY(cudaFuncSetAttribute(w4_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+  {
+    const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(w4_decode_kernel), kSmemBytes);
+    if (st != LMOE_OK) return st;
+  }
   w4_decode_kernel<<<dev.num_sms, kThreads, kSmemBytes, stream>>>(tm_x16, tm_x32, a);
   return cuda_status(cudaGetLastError());
 }

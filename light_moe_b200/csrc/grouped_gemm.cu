@@ -516,7 +516,10 @@ int launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, GemmArgs a, in
   a.tmem_cols = cols;
   const size_t smem = C::kSmemBytes + sizeof(GemmBars);
   auto fn = grouped_gemm_kernel<BN, DQ, WST, BST, AST, ACC, W4, BOX>;
-  LMOE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  {
+    const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+    if (st != LMOE_OK) return st;
+  }
   fn<<<grid, C::kThreads, smem, stream>>>(tm_x, tm_w, a);
   return cuda_status(cudaGetLastError());
 }

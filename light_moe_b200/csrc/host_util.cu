@@ -40,6 +40,36 @@ int get_device_info(DeviceInfo* out) {
   return LMOE_OK;
 }
 
+namespace {
+struct SmemAttr {
+  const void* fn;
+  int device;
+  size_t smem;
+};
+constexpr int kMaxSmemAttrs = 256;
+SmemAttr g_smem_attr[kMaxSmemAttrs];
+int g_smem_attr_n = 0;
+std::mutex g_smem_attr_mu;
+}  // namespace
+
+int set_max_dynamic_smem(const void* fn, size_t smem) {
+  int dev = 0;
+  LMOE_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_smem_attr_mu);
+  int slot = -1;
+  for (int i = 0; i < g_smem_attr_n; ++i) {
+    if (g_smem_attr[i].fn == fn && g_smem_attr[i].device == dev) {
+      if (g_smem_attr[i].smem >= smem) return LMOE_OK;
+      slot = i;
+      break;
+    }
+  }
+  LMOE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (slot < 0 && g_smem_attr_n < kMaxSmemAttrs) slot = g_smem_attr_n++;
+  if (slot >= 0) g_smem_attr[slot] = {fn, dev, smem};   // a full table only loses the shortcut
+  return LMOE_OK;
+}
+
 int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                    uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols,
                    bool swizzle128) {

@@ -37,6 +37,11 @@ struct DeviceInfo {
 
 int get_device_info(DeviceInfo* out);
 
+// cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, smem) on the current device, skipped
+// when this (kernel, device) already allows at least `smem` bytes: the attribute call costs
+// microseconds of host time on every launch otherwise.
+int set_max_dynamic_smem(const void* fn, size_t smem);
+
 // Encode a 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes` bytes,
 // row pitch `row_stride_bytes`, box `box_cols` x `box_rows`, 128-byte swizzle when
 // `swizzle128` (box_cols * elem_bytes must then be 128).  Returns a C-ABI status.

@@ -15,8 +15,9 @@
 // top-2 only, and ~2E+6 ATen launches for counts/offsets/argsort; here it is one kernel.
 //
 // Structure (persistent, one CTA per SM, 128 tokens per tile, 6 warps):
-//   warp 0     TMA producer: x tile [128 x 64] and W tile [Epad x 64] per stage (128B swizzle)
-//   warp 1     MMA issuer: 4 x tcgen05.mma (M=128, N=Epad, K=16) per stage into one of two
+//   warp 0     TMA producer: two x tiles [128 x 64] and two W tiles [Epad x 64] per stage
+//              (128B swizzle; 256 contiguous bytes of every token row per stage)
+//   warp 1     MMA issuer: 8 x tcgen05.mma (M=128, N=Epad, K=16) per stage into one of two
 //              TMEM accumulators
 //   warps 2-5  epilogue: one token row per thread (TMEM lane), softmax / top-k / renormalise,
 //              per-tile expert bitmap for the permutation
@@ -33,8 +34,9 @@
 namespace lmoe {
 namespace {
 
-constexpr int kBM = 128;          // tokens per tile
-constexpr int kBK = 64;           // hidden elements per stage (one 128-byte swizzle row)
+constexpr int kBM = 128;          // MMA rows per tile; a tile holds bm <= kBM tokens (see router_tile_rows)
+constexpr int kBK = 64;           // hidden elements per TMA box (one 128-byte swizzle row)
+constexpr int kBoxes = 2;         // boxes per pipeline stage: 128 hidden elements per stage
 constexpr int kThreads = 192;     // 6 warps
 constexpr int kMaxStages = 8;
 constexpr int kMaxExperts = 256;
@@ -55,7 +57,9 @@ struct RouterArgs {
   uint32_t* grid_sync;    // arrival counter for the grid barrier (zeroed by the host)
   uint32_t* err;          // device error word (zeroed by the host)
   int T, d, E, Epad, k, num_tiles, stages;
-  uint32_t stage_bytes;   // x tile + W tile, multiple of 1024
+  int bm;                 // tokens per tile (multiple of 8, <= kBM); MMA rows >= bm are ignored
+  uint32_t stage_bytes;   // kBoxes x tiles + kBoxes W tiles, multiple of 1024
+  uint32_t w_box_bytes;   // one W tile [Epad x kBK]
   uint32_t tmem_cols;
   int do_perm;
 };
@@ -73,6 +77,15 @@ struct __align__(8) RouterHdr {
   int32_t total[kMaxExperts];
   int32_t offs[kMaxExperts + 1];
 };
+
+__device__ __forceinline__ int32_t warp_inclusive_scan(int32_t v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
@@ -92,7 +105,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int nk = a.d / kBK;
+  const int nk = (a.d + kBK * kBoxes - 1) / (kBK * kBoxes);   // stages per tile
+  constexpr uint32_t kXBox = kBM * kBK * 2;
 
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -133,10 +147,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ph = (it / a.stages) & 1u;
           if (!mbar_wait(&h->empty[s], ph ^ 1u, a.err, abort_flag, kSite + 1)) { ok = false; break; }
           uint8_t* xs = base + s * a.stage_bytes;
-          uint8_t* ws = xs + kBM * kBK * 2;
-          mbar_arrive_expect_tx(&h->full[s], a.stage_bytes);
-          tma_load_2d(xs, &tm_x, &h->full[s], kc * kBK, tile * kBM);
-          tma_load_2d(ws, &tm_w, &h->full[s], kc * kBK, 0);
+          uint8_t* ws = xs + kBoxes * kXBox;
+          const int nb = min(kBoxes, a.d / kBK - kc * kBoxes);   // the last stage may hold one box
+          // an x box is bm rows (bm * 128 bytes, rows past T zero-filled); rows bm..127 of the
+          // slot keep stale bytes, which only reach accumulator rows that are never read
+          mbar_arrive_expect_tx(&h->full[s], (uint32_t)nb * ((uint32_t)a.bm * kBK * 2 + a.w_box_bytes));
+          for (int b = 0; b < nb; ++b) {
+            tma_load_2d(xs + b * kXBox, &tm_x, &h->full[s], (kc * kBoxes + b) * kBK, tile * a.bm);
+            tma_load_2d(ws + b * a.w_box_bytes, &tm_w, &h->full[s], (kc * kBoxes + b) * kBK, 0);
+          }
         }
       }
       // never leave the CTA with bulk copies still landing in shared memory
@@ -163,11 +182,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&h->full[s], (it / a.stages) & 1u, a.err, abort_flag, kSite + 4)) { ok = false; break; }
           tc_fence_after();
           const uint32_t xa = smem_u32(base + s * a.stage_bytes);
-          const uint32_t wa = xa + kBM * kBK * 2;
+          const uint32_t wa = xa + kBoxes * kXBox;
+          const int nb = min(kBoxes, a.d / kBK - kc * kBoxes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            mma_ss(d_tmem, sdesc_k_sw128(xa + kk * 32), sdesc_k_sw128(wa + kk * 32), idesc,
-                   (kc | kk) != 0 ? 1u : 0u);
+          for (int b = 0; b < kBoxes; ++b) {
+            if (b < nb) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                mma_ss(d_tmem, sdesc_k_sw128(xa + b * kXBox + kk * 32),
+                       sdesc_k_sw128(wa + b * a.w_box_bytes + kk * 32), idesc, (kc | b | kk) != 0 ? 1u : 0u);
+              }
+            }
           }
           mma_commit(&h->empty[s]);
         }
@@ -186,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = lt & 1u;
       if (!mbar_wait(&h->acc_full[acc], (lt >> 1) & 1u, a.err, abort_flag, kSite + 6)) break;
       tc_fence_after();
-      const int64_t t = (int64_t)tile * kBM + row;
-      const bool valid = t < a.T;
+      const int64_t t = (int64_t)tile * a.bm + row;
+      const bool valid = row < a.bm && t < a.T;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * a.Epad;
       uint32_t r[16];
       // pass 1: logits (+bias), running max
@@ -295,24 +320,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     if (!*abort_flag) {
-      // per-expert totals and, for each tile owned by this CTA, the count of earlier tiles
+      // per-expert totals and, for each tile owned by this CTA, the count of earlier tiles.
+      // The [num_tiles, E] count table is staged through shared memory in chunks of tiles
+      // (16-byte loads, all of a thread's loads in flight at once); then thread e walks
+      // column e of the chunk in tile order.  Integer sums: the result is order-exact.
+      const int own_max = (a.num_tiles + (int)gridDim.x - 1) / (int)gridDim.x;
       int32_t* pref = reinterpret_cast<int32_t*>(base);  // [own tiles, E] in the stage area
-      for (int e = tid; e < a.E; e += kThreads) {
-        int32_t run = 0;
-        for (int tile = 0; tile < a.num_tiles; ++tile) {
-          if ((tile % (int)gridDim.x) == (int)blockIdx.x) pref[(tile / gridDim.x) * a.E + e] = run;
-          run += __ldcg(&a.tile_counts[(int64_t)tile * a.E + e]);
+      const int pref_ints = (own_max * a.E + 3) & ~3;
+      int32_t* chunk = pref + pref_ints;                 // [chunk tiles, E], 16-byte aligned
+      const int area_ints = (int)(((size_t)a.stages * a.stage_bytes) / 4) - pref_ints;
+      const int chunk_tiles = min(((area_ints / a.E) & ~3), (a.num_tiles + 3) & ~3);   // >= 4 (host)
+      constexpr int kEPer = (kMaxExperts + kThreads - 1) / kThreads;
+      int32_t run[kEPer];
+#pragma unroll
+      for (int j = 0; j < kEPer; ++j) run[j] = 0;
+      for (int c0 = 0; c0 < a.num_tiles; c0 += chunk_tiles) {
+        const int nt = min(chunk_tiles, a.num_tiles - c0);
+        const int n = nt * a.E;
+        const int32_t* src = a.tile_counts + (int64_t)c0 * a.E;   // c0 * E * 4 is 16-byte aligned
+        constexpr int kBatch = 8;
+        for (int i0 = tid * 4; i0 < n; i0 += kThreads * 4 * kBatch) {
+          int4 v[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + u * kThreads * 4;
+            if (i + 3 < n) v[u] = __ldcg(reinterpret_cast<const int4*>(src + i));
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + u * kThreads * 4;
+            if (i + 3 < n) {
+              *reinterpret_cast<int4*>(chunk + i) = v[u];
+            } else {
+              for (int r = i; r < n; ++r) chunk[r] = __ldcg(src + r);   // ragged tail (E % 4 != 0)
+            }
+          }
         }
-        h->total[e] = run;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kEPer; ++j) {
+          const int e = tid + j * kThreads;
+          if (e < a.E) {
+            int32_t r = run[j];
+            int own = (c0 + (int)gridDim.x - 1 - (int)blockIdx.x) / (int)gridDim.x;   // owned tiles before c0
+            int next = (int)blockIdx.x + own * (int)gridDim.x;                      // next owned tile
+            for (int tt = 0; tt < nt; ++tt) {
+              const int tile = c0 + tt;
+              if (tile == next) {
+                pref[own * a.E + e] = r;
+                ++own;
+                next += (int)gridDim.x;
+              }
+              r += chunk[tt * a.E + e];
+            }
+            run[j] = r;
+          }
+        }
+        __syncthreads();
+      }
+#pragma unroll
+      for (int j = 0; j < kEPer; ++j) {
+        const int e = tid + j * kThreads;
+        if (e < a.E) h->total[e] = run[j];
       }
       __syncthreads();
-      if (tid == 0) {
-        int32_t off = 0;
-        for (int e = 0; e < a.E; ++e) {
-          h->offs[e] = off;
-          off += h->total[e];
+      // exclusive scan of the per-expert totals: warp 0, 32 experts per round
+      if (warp == 0) {
+        int32_t run = 0;
+        for (int e0 = 0; e0 < a.E; e0 += 32) {
+          const int e = e0 + lane;
+          const int32_t c = e < a.E ? h->total[e] : 0;
+          const int32_t v = warp_inclusive_scan(c, lane);
+          if (e < a.E) h->offs[e] = run + v - c;
+          run += __shfl_sync(0xffffffffu, v, 31);
         }
-        h->offs[a.E] = off;
+        if (lane == 0) h->offs[a.E] = run;
       }
       __syncthreads();
       if (blockIdx.x == 0) {
@@ -324,20 +406,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int own = 0;
       for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++own) {
-        for (int row = tid; row < kBM; row += kThreads) {
-          const int64_t t = (int64_t)tile * kBM + row;
+        for (int row = tid; row < a.bm; row += kThreads) {
+          const int64_t t = (int64_t)tile * a.bm + row;
           if (t >= a.T) continue;
           const int w = row >> 5;
           const uint32_t below = (1u << (row & 31)) - 1u;
-          for (int j = 0; j < a.k; ++j) {
-            const int e = a.ids[t * a.k + j];
-            const uint4 bv = __ldcg(reinterpret_cast<const uint4*>(a.tile_bits) + (int64_t)tile * a.E + e);
-            const uint32_t b[4] = {bv.x, bv.y, bv.z, bv.w};
-            int rank = __popc(b[w] & below);
-            for (int i = 0; i < w; ++i) rank += __popc(b[i]);
-            const int32_t pos = h->offs[e] + pref[own * a.E + e] + rank;
-            a.sorted_idx[pos] = (int32_t)(t * a.k + j);
-            if (a.positions) a.positions[t * a.k + j] = pos;
+          // the row's k expert ids, then their k tile bitmaps: two rounds of loads in flight
+          int ev[KMAX];
+          uint4 bv[KMAX];
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j)
+            if (j < a.k) ev[j] = __ldcg(&a.ids[t * a.k + j]);
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j)
+            if (j < a.k) bv[j] = __ldcg(reinterpret_cast<const uint4*>(a.tile_bits) + (int64_t)tile * a.E + ev[j]);
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) {
+            if (j < a.k) {
+              const uint32_t b[4] = {bv[j].x, bv[j].y, bv[j].z, bv[j].w};
+              int rank = __popc(b[w] & below);
+#pragma unroll
+              for (int i = 0; i < 3; ++i)
+                if (i < w) rank += __popc(b[i]);
+              const int32_t pos = h->offs[ev[j]] + pref[own * a.E + ev[j]] + rank;
+              a.sorted_idx[pos] = (int32_t)(t * a.k + j);
+              if (a.positions) a.positions[t * a.k + j] = pos;
+            }
           }
         }
       }
@@ -462,11 +556,34 @@ __global__ void __launch_bounds__(kSmallTokens) router_small_route_kernel(const 
   }
 }
 
+// Tile height: 128 tokens, or fewer when there are fewer than 128 tokens per SM, so that
+// every SM streams a share of x (a multiple of 8 rows: whole 128-byte swizzle atoms).
+// The SM count is capped at kMaxGridTiles so the tile count stays bounded without
+// querying the device (router_max_tiles, used for the workspace size).
+constexpr int kMaxGridTiles = 256;
+
+int router_tile_rows(int64_t T, int num_sms) {
+  const int64_t s = num_sms < kMaxGridTiles ? num_sms : kMaxGridTiles;
+  int64_t bm = (T + s - 1) / s;
+  bm = (bm + 7) & ~int64_t(7);
+  return (int)(bm > kBM ? kBM : (bm < 8 ? 8 : bm));
+}
+
+// Upper bound on ceil(T / router_tile_rows(T, any SM count)).
+constexpr int64_t router_max_tiles(int64_t T) {
+  const int64_t full = (T + kBM - 1) / kBM;
+  const int64_t small = (T + 7) / 8 < kMaxGridTiles ? (T + 7) / 8 : kMaxGridTiles;
+  return full > small ? full : small;
+}
+
 template <int KMAX>
 int launch_router(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const RouterArgs& a, int grid, size_t smem,
                   cudaStream_t stream) {
   auto fn = router_kernel<KMAX>;
-  LMOE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  {
+    const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+    if (st != LMOE_OK) return st;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -488,8 +605,8 @@ int launch_router(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const Router
 // ---------------------------------------------------------------------------------------
 constexpr int64_t kStaticMaxTokens = 16384;
 constexpr size_t kStaticScratchBytes =
-    ((256 + (size_t)((kStaticMaxTokens + kBM - 1) / kBM) * kMaxExperts * sizeof(int32_t) + 255) & ~size_t(255)) +
-    (size_t)((kStaticMaxTokens + kBM - 1) / kBM) * kMaxExperts * 4 * sizeof(uint32_t);   // 640 KB + 256 B
+    ((256 + (size_t)router_max_tiles(kStaticMaxTokens) * kMaxExperts * sizeof(int32_t) + 255) & ~size_t(255)) +
+    (size_t)router_max_tiles(kStaticMaxTokens) * kMaxExperts * 4 * sizeof(uint32_t);   // 1.25 MB + 256 B
 
 static __device__ __align__(256) uint8_t g_router_scratch[kStaticScratchBytes];
 
@@ -522,7 +639,7 @@ using namespace lmoe;
 
 extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts) {
   if (num_tokens < 0 || num_experts <= 0) return 0;
-  const int64_t tiles = (num_tokens + kBM - 1) / kBM;
+  const int64_t tiles = router_max_tiles(num_tokens);
   size_t bytes = 256;                                   // error word + grid barrier counter
   bytes += (size_t)tiles * num_experts * sizeof(int32_t);
   bytes = (bytes + 255) & ~size_t(255);
@@ -590,8 +707,10 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
     return cuda_status(cudaGetLastError());
   }
   const int Epad = ((E + 15) / 16) * 16;
-  const int num_tiles = (int)((num_tokens + kBM - 1) / kBM);
-  const uint32_t stage_bytes = kBM * kBK * 2 + Epad * kBK * 2;
+  const int bm = router_tile_rows(num_tokens, dev.num_sms);
+  const int num_tiles = (int)((num_tokens + bm - 1) / bm);
+  const uint32_t w_box_bytes = (uint32_t)Epad * kBK * 2;           // multiple of 2048
+  const uint32_t stage_bytes = kBoxes * (kBM * kBK * 2 + w_box_bytes);
   const size_t hdr = (sizeof(RouterHdr) + 1023) & ~size_t(1023);
   int stages = (int)((dev.max_smem_optin - hdr - 1024) / stage_bytes);
   stages = stages > kMaxStages ? kMaxStages : stages;
@@ -601,8 +720,10 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   while (tmem_cols < (uint32_t)(2 * Epad)) tmem_cols <<= 1;
   const int grid = num_tiles < dev.num_sms ? num_tiles : dev.num_sms;
   if (do_perm) {
-    const int own_max = (num_tiles + grid - 1) / grid;
-    if ((size_t)own_max * E * sizeof(int32_t) > (size_t)stages * stage_bytes) return LMOE_ERR_UNSUPPORTED;
+    // the stage area holds the owned tiles' prefixes and a chunk of at least 4 count rows
+    const size_t own_max = (size_t)((num_tiles + grid - 1) / grid);
+    const size_t pref_ints = (own_max * E + 3) & ~size_t(3);
+    if ((pref_ints + 4 * (size_t)E) * sizeof(int32_t) > (size_t)stages * stage_bytes) return LMOE_ERR_UNSUPPORTED;
   }
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -628,15 +749,17 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   a.E = E;
   a.Epad = Epad;
   a.k = top_k;
+  a.bm = bm;
   a.num_tiles = num_tiles;
   a.stages = stages;
   a.stage_bytes = stage_bytes;
+  a.w_box_bytes = w_box_bytes;
   a.tmem_cols = tmem_cols;
   a.do_perm = do_perm ? 1 : 0;
 
   CUtensorMap tm_x, tm_w;
   st = encode_tmap_2d(&tm_x, hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)num_tokens,
-                      (uint64_t)hidden_size, (uint64_t)hidden_size * 2, kBM, kBK, true);
+                      (uint64_t)hidden_size, (uint64_t)hidden_size * 2, (uint32_t)bm, kBK, true);
   if (st != LMOE_OK) return st;
   st = encode_tmap_2d(&tm_w, gate_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E, (uint64_t)hidden_size,
                       (uint64_t)hidden_size * 2, (uint32_t)Epad, kBK, true);

@@ -47,8 +47,11 @@ def test_host_only_entry_points():
     assert lib.lmoe_version() >= 100
     assert lib.lmoe_status_string(0) == b"ok"
     assert b"workspace" in lib.lmoe_status_string(capi.LMOE_ERR_WORKSPACE)
-    # router scratch: 256 B header + per-tile counts + per-tile bitmaps
-    assert lib.lmoe_router_workspace_bytes(16384, 64) == 256 + 128 * 64 * 4 + 128 * 64 * 16
+    # router scratch: 256 B header + per-tile counts + per-tile bitmaps, for at most
+    # max(ceil(T/128), min(ceil(T/8), 256)) tiles (tiles shrink below 128 tokens to fill the SMs)
+    assert lib.lmoe_router_workspace_bytes(16384, 64) == 256 + 256 * 64 * 4 + 256 * 64 * 16
+    assert lib.lmoe_router_workspace_bytes(65536, 8) == 256 + 512 * 8 * 4 + 512 * 8 * 16
+    assert lib.lmoe_router_workspace_bytes(1000, 8) == (256 + 125 * 8 * 4 + 255) // 256 * 256 + 125 * 8 * 16
     assert lib.lmoe_router_workspace_bytes(-1, 8) == 0
     nb = ctypes.c_size_t()
     # Mixtral gate/up: 8 experts, 2 x 14336 rows x 4096 K, g=128: 8192 B int4 + 256 B scales per super-block

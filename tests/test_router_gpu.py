@@ -42,10 +42,14 @@ def _logit_bound(x, w):
 
 
 # T <= 128 runs the small-batch path (warp dot products + one routing CTA), larger T the
-# tensor-core kernel; (128, ...) and (129, ...) sit on either side of the switch
+# tensor-core kernel; (128, ...) and (129, ...) sit on either side of the switch.  Below
+# 128 tokens per SM the tiles shrink (8..120 rows); (40000, ...) gives several 128-token
+# tiles per CTA, (50000, 64, 256, ...) a count table staged in several chunks, (400, 192,
+# 7, ...) a ragged count row (E % 4 != 0) and a stage holding one 64-wide box.
 @pytest.mark.parametrize("T,d,E,k", [(1, 64, 8, 2), (64, 4096, 8, 2), (257, 128, 16, 4), (300, 256, 64, 6),
                                      (1000, 512, 8, 1), (129, 64, 256, 16), (77, 192, 40, 7), (512, 1024, 64, 8),
-                                     (128, 256, 256, 16), (128, 128, 8, 2)])
+                                     (128, 256, 256, 16), (128, 128, 8, 2), (400, 192, 7, 3),
+                                     (40000, 256, 64, 6), (50000, 64, 256, 8)])
 def test_router_bitexact_given_logits(T, d, E, k):
     x, w = _inputs(T, d, E, seed=T + E)
     out = router(x, w, k)
@@ -104,7 +108,7 @@ def test_router_ties_go_to_lower_expert_id():
     assert out0["ids"].tolist() == [[0, 1, 2]] * 4
 
 
-@pytest.mark.parametrize("T,d,E,k", [(64, 1024, 8, 2), (300, 256, 16, 4)])
+@pytest.mark.parametrize("T,d,E,k", [(64, 1024, 8, 2), (300, 256, 16, 4), (30000, 128, 64, 6)])
 def test_router_positions_invert_the_permutation(T, d, E, k):
     x, w = _inputs(T, d, E, seed=19 + T)
     out = router(x, w, k, positions=True)
