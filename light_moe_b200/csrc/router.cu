@@ -14,13 +14,15 @@
 // after two dtype-conversion copies, a CUDA-core softmax/top-k kernel for E in {8,16} and
 // top-2 only, and ~2E+6 ATen launches for counts/offsets/argsort; here it is one kernel.
 //
-// Structure (persistent, one CTA per SM, 128 tokens per tile, 6 warps):
+// Structure (persistent, one CTA per SM, up to 128 tokens per tile, 10 warps):
 //   warp 0     TMA producer: two x tiles [128 x 64] and two W tiles [Epad x 64] per stage
 //              (128B swizzle; 256 contiguous bytes of every token row per stage)
 //   warp 1     MMA issuer: 8 x tcgen05.mma (M=128, N=Epad, K=16) per stage into one of two
 //              TMEM accumulators
 //   warps 2-5  epilogue: one token row per thread (TMEM lane), softmax / top-k / renormalise,
 //              per-tile expert bitmap for the permutation
+//   warps 6-9  epilogue helpers (more than 16 experts): the upper half of each row's expert
+//              columns (exponentials, partial top-k), exchanged through shared memory
 // When the permutation is requested the kernel is launched cooperatively and, after a grid
 // barrier, every CTA scans the per-tile counts and scatters its tokens into sorted_idx.
 #include <cuda_bf16.h>
@@ -37,7 +39,9 @@ namespace {
 constexpr int kBM = 128;          // MMA rows per tile; a tile holds bm <= kBM tokens (see router_tile_rows)
 constexpr int kBK = 64;           // hidden elements per TMA box (one 128-byte swizzle row)
 constexpr int kBoxes = 2;         // boxes per pipeline stage: 128 hidden elements per stage
-constexpr int kThreads = 192;     // 6 warps
+constexpr int kEpiWarps = 4;      // epilogue warps that own the token rows (one per TMEM lane quarter)
+constexpr int kThreads = 64 + 2 * 32 * kEpiWarps;   // producer, MMA issuer, owners, helpers: 10 warps
+constexpr uint32_t kEpiAllBar = 6;   // named barrier of all epilogue threads (ids 1-5: owners, pairs)
 constexpr int kMaxStages = 8;
 constexpr int kMaxExperts = 256;
 constexpr uint32_t kSite = 0x100u;
@@ -100,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   RouterHdr* h = reinterpret_cast<RouterHdr*>(base + a.stages * a.stage_bytes);
+  uint8_t* xchg = reinterpret_cast<uint8_t*>(h + 1);   // owner / helper exchange (split epilogue only)
   volatile int* abort_flag = &h->abort;
 
   const int tid = threadIdx.x;
@@ -204,20 +209,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;          // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;   // token row within the tile
+    // Warp w serves TMEM lane quarter w & 3.  Warps 2-5 own the token rows; when the experts
+    // span more than one 16-column chunk, warps 6-9 take the upper chunks of the same rows
+    // (exponentials and a partial top-k), so each pass has two threads per row.
+    const int q = warp & 3;
+    const int row = q * 32 + lane;           // token row within the tile
+    const bool owner = warp < 2 + kEpiWarps;
+    const int nch = a.Epad / 16;
+    const bool split = nch >= 2;
+    const int ch_a = split ? (nch + 1) / 2 : nch;   // chunks [0, ch_a) to the owner
+    const int c_lo = owner ? 0 : ch_a * 16;
+    const int c_hi = owner ? ch_a * 16 : a.Epad;
+    const uint32_t pair_bar = 2 + q;         // the owner warp and its helper (64 threads)
+    const uint32_t epi_threads = split ? 2 * 32 * kEpiWarps : 32 * kEpiWarps;
+    float* x_m = reinterpret_cast<float*>(xchg);                  // [2][128]
+    float* x_inv = x_m + 2 * kBM;                                 // [128]
+    float* x_tv = x_inv + kBM;                                    // [KMAX][128]
+    int* x_ti = reinterpret_cast<int*>(x_tv + KMAX * kBM);        // [KMAX][128]
     uint32_t lt = 0;
-    for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++lt) {
+    for (int tile = blockIdx.x; (owner || split) && tile < a.num_tiles; tile += gridDim.x, ++lt) {
       const uint32_t acc = lt & 1u;
-      if (!mbar_wait(&h->acc_full[acc], (lt >> 1) & 1u, a.err, abort_flag, kSite + 6)) break;
+      // every epilogue thread leaves together if any of them gave up waiting
+      const bool fail = !mbar_wait(&h->acc_full[acc], (lt >> 1) & 1u, a.err, abort_flag, kSite + 6);
+      if (named_bar_any(kEpiAllBar, epi_threads, fail)) break;
       tc_fence_after();
       const int64_t t = (int64_t)tile * a.bm + row;
       const bool valid = row < a.bm && t < a.T;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * a.Epad;
       uint32_t r[16];
-      // pass 1: logits (+bias), running max
+      // pass 1: logits (+bias), running max over this thread's chunks
       float m = -INFINITY;
-      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         tmem_ld16(taddr + c0, r);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -229,38 +251,78 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // pass 2: sum of exp(l - max), sequential over experts
-      float sum = 0.0f;
-      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+      if (split) {   // the maximum is exact in any order
+        x_m[(owner ? 0 : kBM) + row] = m;
+        named_bar_sync(pair_bar, 64);
+        m = fmaxf(x_m[row], x_m[kBM + row]);
+      }
+      // pass 2: exp(l - max) of this thread's chunks, written back over the logits
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         tmem_ld16(taddr + c0, r);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int e = c0 + i;
-          if (e < a.E) {
-            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
-            sum = __fadd_rn(sum, softmax_exp(__fsub_rn(l, m)));
-          }
+          const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e < a.E ? e : 0]);
+          r[i] = e < a.E ? __float_as_uint(softmax_exp(__fsub_rn(l, m))) : 0u;
         }
+        tmem_st16(taddr + c0, r);
       }
-      const float inv = __frcp_rn(sum);
-      // pass 3: probabilities and top-k
+      tmem_wait_st();
+      if (split) {
+        tc_fence_before();
+        named_bar_sync(pair_bar, 64);
+        tc_fence_after();
+      }
+      // the owner sums all exponentials sequentially over experts 0..E-1
+      float inv = 0.0f;
+      if (owner) {
+        float sum = 0.0f;
+        for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+          tmem_ld16(taddr + c0, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < a.E) sum = __fadd_rn(sum, __uint_as_float(r[i]));
+        }
+        inv = __frcp_rn(sum);
+      }
+      if (split) {
+        if (owner) x_inv[row] = inv;
+        named_bar_sync(pair_bar, 64);
+        if (!owner) inv = x_inv[row];
+      }
+      // pass 3: probabilities and top-k over this thread's chunks
       float tv[KMAX];
       int ti[KMAX];
 #pragma unroll
       for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
-      for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         tmem_ld16(taddr + c0, r);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int e = c0 + i;
-          if (e < a.E) {
-            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
-            const float p = __fmul_rn(softmax_exp(__fsub_rn(l, m)), inv);
-            topk_insert<KMAX>(tv, ti, p, e);
-          }
+          if (e < a.E) topk_insert<KMAX>(tv, ti, __fmul_rn(__uint_as_float(r[i]), inv), e);
         }
       }
-      // the accumulator can be reused by the MMA warp
+      if (split) {
+        // the helper's list (higher expert ids, descending) is inserted after the owner's:
+        // the merged list equals the sequential insertion over all experts
+        tc_fence_before();
+        if (!owner) {
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) {
+            x_tv[j * kBM + row] = tv[j];
+            x_ti[j * kBM + row] = ti[j];
+          }
+        }
+        named_bar_sync(pair_bar, 64);
+        if (owner) {
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) topk_insert<KMAX>(tv, ti, x_tv[j * kBM + row], x_ti[j * kBM + row]);
+        }
+      }
+      if (!owner) continue;
+      // the accumulator can be reused by the MMA warp (the helper finished reading it
+      // before the last pair barrier)
       tc_fence_before();
       mbar_arrive(&h->acc_empty[acc]);
       float ssum = 0.0f;
@@ -281,8 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (a.do_perm) {
-        named_bar_sync(1, 128);
-        for (int e = row; e < a.E; e += 128) {
+        named_bar_sync(1, 32 * kEpiWarps);
+        for (int e = row; e < a.E; e += kBM) {
           uint32_t b[4];
           int cnt = 0;
 #pragma unroll
@@ -295,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 bv = make_uint4(b[0], b[1], b[2], b[3]);
           reinterpret_cast<uint4*>(a.tile_bits)[(int64_t)tile * a.E + e] = bv;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * kEpiWarps);
       }
     }
   }
@@ -711,11 +773,15 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   const int num_tiles = (int)((num_tokens + bm - 1) / bm);
   const uint32_t w_box_bytes = (uint32_t)Epad * kBK * 2;           // multiple of 2048
   const uint32_t stage_bytes = kBoxes * (kBM * kBK * 2 + w_box_bytes);
-  const size_t hdr = (sizeof(RouterHdr) + 1023) & ~size_t(1023);
+  // header, then (more than one 16-column chunk of experts) the owner / helper exchange:
+  // max [2][128], 1/sum [128], partial top-k values and ids [KMAX][128] each
+  const int kmax = top_k <= 2 ? 2 : top_k <= 4 ? 4 : top_k <= 8 ? 8 : 16;
+  const size_t xchg = Epad > 16 ? (size_t)(3 + 2 * kmax) * kBM * 4 : 0;
+  const size_t hdr = (sizeof(RouterHdr) + xchg + 1023) & ~size_t(1023);
   int stages = (int)((dev.max_smem_optin - hdr - 1024) / stage_bytes);
   stages = stages > kMaxStages ? kMaxStages : stages;
   if (stages < 2) return LMOE_ERR_UNSUPPORTED;
-  const size_t smem = 1024 + (size_t)stages * stage_bytes + sizeof(RouterHdr);
+  const size_t smem = 1024 + (size_t)stages * stage_bytes + sizeof(RouterHdr) + xchg;
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * Epad)) tmem_cols <<= 1;
   const int grid = num_tiles < dev.num_sms ? num_tiles : dev.num_sms;
