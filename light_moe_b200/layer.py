@@ -17,6 +17,11 @@ import torch
 
 from . import ops
 
+# Batches of at most this many tokens take other kernels than larger ones: the CUDA-core
+# router (csrc/router.cu, kSmallTokens = 128; its fp32 dot products round differently from
+# the tensor-core logits) and, at 64 tokens or fewer, the decode GEMMs (csrc/layer.cu).
+SMALL_BATCH_TOKENS = 128
+
 
 @dataclass
 class W4A16Experts:
@@ -84,3 +89,66 @@ class W4A16MoELayer(torch.nn.Module):
                                         e.ffn_size, e.group_size, e.num_shared, self.gate_bias)
         y = y.view(*shape[:-1], shape[-1])
         return (y, ids, w) if return_routing else y
+
+    def forward_host(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     chunks: Optional[int] = None) -> torch.Tensor:
+        """The layer on host-resident activations: x_host [..., d] bf16 on the CPU (pinned for
+        asynchronous copies) in, y written to ``out`` (pinned host [..., d], allocated if None).
+
+        The tokens are split into ``chunks`` contiguous ranges (default: one per 2560 tokens,
+        at most 4: smaller ranges leave the GEMMs' 192-token tiles partly empty, which costs
+        more than the copies they hide); the host-to-device copy of
+        range c + 1 and the device-to-host copy of range c - 1 run on copy streams while
+        range c is computed, so the PCIe transfers hide behind the kernels.  Every token's
+        output depends on that token alone and every range keeps more than
+        ``SMALL_BATCH_TOKENS`` tokens (a batch that small is one range), so each range runs
+        the same kernels as the whole batch would and the result is bit-identical to
+        ``forward(x_host.cuda()).cpu()``.  Returns ``out``; it is complete once the current
+        CUDA stream has reached the point of return (synchronise before reading it).
+        """
+        if x_host.device.type != "cpu":
+            raise ValueError("forward_host takes host activations; use forward for device tensors")
+        if x_host.dtype != torch.bfloat16:
+            raise ValueError("activations must be bf16")
+        shape = x_host.shape
+        x2 = x_host.reshape(-1, shape[-1])
+        if out is None:
+            out = torch.empty(shape, dtype=torch.bfloat16, pin_memory=True)
+        elif out.shape != shape or out.dtype != torch.bfloat16 or out.device.type != "cpu":
+            raise ValueError("out must be a bf16 host tensor shaped like x_host")
+        if not out.is_contiguous():
+            raise ValueError("out must be contiguous")
+        y2 = out.view(-1, shape[-1])
+        T = x2.shape[0]
+        device = self.gate_weight.device
+        cur = torch.cuda.current_stream(device)
+        if T == 0:
+            return out
+        if chunks is None:
+            chunks = min(4, T // 2560)
+        n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
+        bounds = [T * i // n for i in range(n + 1)]
+        if not hasattr(self, "_copy_streams"):
+            self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        h2d, d2h = self._copy_streams
+        xd = torch.empty((T, shape[-1]), dtype=torch.bfloat16, device=device)
+        h2d.wait_stream(cur)            # xd's memory is free on the current stream from here
+        loaded = []
+        with torch.cuda.stream(h2d):
+            for i in range(n):
+                a, b = bounds[i], bounds[i + 1]
+                xd[a:b].copy_(x2[a:b], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                loaded.append(ev)
+        xd.record_stream(h2d)
+        for i in range(n):
+            a, b = bounds[i], bounds[i + 1]
+            cur.wait_event(loaded[i])
+            yc = self.forward(xd[a:b])
+            d2h.wait_stream(cur)
+            with torch.cuda.stream(d2h):
+                y2[a:b].copy_(yc, non_blocking=True)
+            yc.record_stream(d2h)
+        cur.wait_stream(d2h)
+        return out

@@ -112,3 +112,24 @@ def test_layer_fine_grained_shape():
     y, ids, wts = mod(x, return_routing=True)
     d1, d3, d2 = _deq(ex)
     _check(y, _ref_torch(x, ids, wts, d1, d3, d2, E))
+
+
+@pytest.mark.parametrize("T,chunks", [(50, 4), (300, 3), (1000, 4), (1000, 16), (4097, 4), (129, 2), (258, 2)])
+def test_forward_host_matches_forward(T, chunks):
+    """Host-buffer layer call (chunked, copies overlapped with the kernels) == device call."""
+    d, F, E, k, g = 256, 256, 8, 2, 128
+    x, gw, ex, _ = _make(T, d, F, E, k, g, seed=3 + T)
+    mod = W4A16MoELayer(gw, ex, k)
+    y_dev = mod(x).cpu()
+    xh = x.cpu().pin_memory()
+    yh = mod.forward_host(xh, chunks=chunks)
+    torch.cuda.synchronize()
+    assert yh.is_pinned()
+    assert torch.equal(yh.view(torch.int16), y_dev.view(torch.int16))
+    # caller-provided output buffer, 3-D activations
+    out = torch.empty((1, T, d), dtype=torch.bfloat16).pin_memory()
+    mod.forward_host(xh.view(1, T, d), out=out, chunks=chunks)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(T, d).view(torch.int16), y_dev.view(torch.int16))
+    with pytest.raises(ValueError):
+        mod.forward_host(x, chunks=chunks)   # device input belongs to forward
