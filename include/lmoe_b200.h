@@ -78,7 +78,7 @@ int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const floa
                          void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
 
 /* lmoe_fused_gate_topk without a workspace argument (no counterpart in the reference): the
- * scratch lives in a fixed 640 KB device array inside this library, for callers that may
+ * scratch lives in a fixed 1.25 MB device array inside this library, for callers that may
  * not allocate device memory (an allocator that owns all device memory, a serving loop that
  * forbids allocation after start-up).
  *   - num_tokens <= 16384 (any num_experts <= 256); larger calls return LMOE_ERR_WORKSPACE.
