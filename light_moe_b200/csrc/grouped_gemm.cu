@@ -89,7 +89,12 @@ struct Cfg {
   static constexpr uint32_t kBStageBytes = 2u * BN * kBK * 2;                        // [2][BN][64] bf16
   static constexpr uint32_t kWStageBytes = W4 ? (uint32_t)(kW4SuperInt4Bytes + 512)  // int4 + <= 2 scale groups
                                               : (uint32_t)(2 * kBM * kBK * 2);       // bf16 [2][128][64]
-  static constexpr uint32_t kXchgBytes = 64 * 17 * 4;
+  // epilogue scratch: SwiGLU exchange buffers of [64 features][32 columns + 1] fp32 (two for
+  // the W4 configurations, so one barrier per 32 columns; one for bf16, whose weight stages
+  // leave less room), then the tile's routing weights and destination rows [BN] each
+  static constexpr int kXchgBufs = W4 ? 2 : 1;
+  static constexpr int kXchgFloats = kXchgBufs * 64 * 33;
+  static constexpr uint32_t kXchgBytes = (uint32_t)kXchgFloats * 4 + BN * 8;
   static constexpr uint32_t kSmemBytes = 1024 + BST * kBStageBytes + WST * kWStageBytes + kXchgBytes + 1024;
   static constexpr uint32_t kTmemColsNeeded = ACC * BN + (W4 ? AST * 64 : 0);
   // dequantise a whole stage into registers before waiting for its TMEM stage when the
@@ -441,9 +446,16 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
     }
   } else if (warp >= C::kEpiWarp0) {
     // ------------------------------------------------------------------ epilogue
+    // 32 accumulator columns (tokens) per step under one TMEM load wait.  SwiGLU: the gate
+    // rows (TMEM lanes 0-63) hand the gate values of columns 16-31 to the up rows (lanes
+    // 64-127), which hand back the up values of columns 0-15, so all four warps compute and
+    // store.  Scatter: the tile's routing weights and destination rows are staged in shared
+    // memory once per tile.
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    uint32_t lt = 0;
+    float* tscale = xchg + C::kXchgFloats;                        // [BN]
+    int32_t* tdest = reinterpret_cast<int32_t*>(tscale + BN);     // [BN]
+    uint32_t lt = 0, chunk = 0;
     int e_hint = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++lt) {
       const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
@@ -453,41 +465,56 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
       const int feat = ti.fb * kBM + row;
-      for (int c0 = 0; c0 < n_eff; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + c0, v);
+      if (a.mode == kModeScatter) {
+        named_bar_sync(2, 128);   // the previous tile's tables are no longer read
+        for (int c = row; c < ti.rows; c += 128) {
+          const int r = ti.row0 + c;
+          tscale[c] = a.row_scale ? a.row_scale[r] : 1.0f;
+          tdest[c] = a.dest ? a.dest[r] : r;
+        }
+        named_bar_sync(2, 128);
+      }
+      for (int c0 = 0; c0 < n_eff; c0 += 32, ++chunk) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16x2(taddr + c0, taddr + c0 + 16, v0, v1);   // c0 + 32 <= BN: inside the buffer
         if (a.mode == kModeSwiGLU) {
-          if (q >= 2) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) xchg[(row - 64) * 17 + i] = __uint_as_float(v[i]);
-          }
-          named_bar_sync(2, 128);
+          float* xb = xchg + (C::kXchgBufs == 2 ? (int)(chunk & 1u) * (64 * 33) : 0);
+          const int f = q < 2 ? row : row - 64;   // feature within the tile's 64
           if (q < 2) {
-            const int f = ti.fb * 64 + row;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int c = c0 + i;
-              if (c < ti.rows) {
-                const float g = __uint_as_float(v[i]);
-                const float u = xchg[row * 17 + i];
-                a.out[(int64_t)(ti.row0 + c) * a.ldo + f] = __float2bfloat16_rn(silu_f(g) * u);
-              }
-            }
+            for (int i = 0; i < 16; ++i) xb[f * 33 + 16 + i] = __uint_as_float(v1[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[f * 33 + i] = __uint_as_float(v0[i]);
           }
           named_bar_sync(2, 128);
-        } else if (feat < a.N) {
+          const int cb = c0 + (q < 2 ? 0 : 16);
+          const int fo = ti.fb * 64 + f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int c = c0 + i;
+            const int c = cb + i;
             if (c < ti.rows) {
-              const int r = ti.row0 + c;
-              float val = __uint_as_float(v[i]);
-              int64_t orow = r;
-              if (a.mode == kModeScatter) {
-                if (a.row_scale) val = __fmul_rn(val, a.row_scale[r]);
-                if (a.dest) orow = a.dest[r];
+              const float g = q < 2 ? __uint_as_float(v0[i]) : xb[f * 33 + 16 + i];
+              const float u = q < 2 ? xb[f * 33 + i] : __uint_as_float(v1[i]);
+              a.out[(int64_t)(ti.row0 + c) * a.ldo + fo] = __float2bfloat16_rn(silu_f(g) * u);
+            }
+          }
+          if (C::kXchgBufs == 1) named_bar_sync(2, 128);   // single buffer: reads done before reuse
+        } else if (feat < a.N) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int c = c0 + 16 * h + i;
+              if (c < ti.rows) {
+                float val = __uint_as_float(h ? v1[i] : v0[i]);
+                int64_t orow = ti.row0 + c;
+                if (a.mode == kModeScatter) {
+                  if (a.row_scale) val = __fmul_rn(val, tscale[c]);
+                  orow = tdest[c];
+                }
+                a.out[orow * a.ldo + feat] = __float2bfloat16_rn(val);
               }
-              a.out[orow * a.ldo + feat] = __float2bfloat16_rn(val);
             }
           }
         }
