@@ -73,6 +73,7 @@ struct GemmArgs {
   const float* row_scale;
   uint32_t* err;
   uint32_t tmem_cols;
+  int vec_out;                // plain / scatter: N % 128 == 0, ldo % 8 == 0, out 16-byte aligned
 };
 
 constexpr int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
@@ -500,6 +501,32 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
             }
           }
           if (C::kXchgBufs == 1) named_bar_sync(2, 128);   // single buffer: reads done before reuse
+        } else if (a.vec_out) {
+          // stage the 32 x 128 output block in shared memory (token-major), then write whole
+          // 256-byte token rows with 16-byte stores instead of 64 bytes per store
+          __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(xchg);   // [32][128], 8 KB
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int c = 16 * h + i;
+              float val = __uint_as_float(h ? v1[i] : v0[i]);
+              if (a.mode == kModeScatter && a.row_scale && c0 + c < ti.rows) val = __fmul_rn(val, tscale[c0 + c]);
+              stg[c * kBM + row] = __float2bfloat16_rn(val);
+            }
+          }
+          named_bar_sync(2, 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int idx = row + 128 * j;    // 16-byte piece: token idx / 16, features 8 * (idx % 16) ..
+            const int c = idx >> 4;
+            if (c0 + c < ti.rows) {
+              const int64_t orow = a.mode == kModeScatter ? (int64_t)tdest[c0 + c] : (int64_t)(ti.row0 + c0 + c);
+              *reinterpret_cast<uint4*>(a.out + orow * a.ldo + ti.fb * kBM + (idx & 15) * 8) =
+                  *reinterpret_cast<const uint4*>(stg + c * kBM + (idx & 15) * 8);
+            }
+          }
+          named_bar_sync(2, 128);   // the stage is rewritten by the next 32 columns
         } else if (feat < a.N) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -593,6 +620,8 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.dest = p.dest;
   a.row_scale = p.row_scale;
   a.err = p.err;
+  a.vec_out = (p.mode != kModeSwiGLU && p.N % kBM == 0 && p.ldo % 8 == 0 &&
+               (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) ? 1 : 0;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
   // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),
