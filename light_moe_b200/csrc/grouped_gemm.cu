@@ -73,7 +73,7 @@ struct GemmArgs {
   const float* row_scale;
   uint32_t* err;
   uint32_t tmem_cols;
-  int vec_out;                // plain / scatter: N % 128 == 0, ldo % 8 == 0, out 16-byte aligned
+  int vec_out;                // N % 128 == 0, ldo % 8 == 0, out 16-byte aligned: staged 16-byte stores
 };
 
 constexpr int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
@@ -478,7 +478,37 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
       for (int c0 = 0; c0 < n_eff; c0 += 32, ++chunk) {
         uint32_t v0[16], v1[16];
         tmem_ld16x2(taddr + c0, taddr + c0 + 16, v0, v1);   // c0 + 32 <= BN: inside the buffer
-        if (a.mode == kModeSwiGLU) {
+        if (a.mode == kModeSwiGLU && C::kXchgBufs == 2 && a.vec_out) {
+          // as below with one exchange buffer, the 32 x 64 bf16 results staged in shared memory
+          // (token-major) and written as whole 128-byte token rows with 16-byte stores
+          float* xb = xchg;                                                     // [64][33]
+          __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(xchg + 64 * 33);   // [32][64], 4 KB
+          const int f = q < 2 ? row : row - 64;
+          if (q < 2) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[f * 33 + 16 + i] = __uint_as_float(v1[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[f * 33 + i] = __uint_as_float(v0[i]);
+          }
+          named_bar_sync(2, 128);
+          const int cl = q < 2 ? 0 : 16;   // this thread's 16 columns within the 32
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float g = q < 2 ? __uint_as_float(v0[i]) : xb[f * 33 + 16 + i];
+            const float u = q < 2 ? xb[f * 33 + i] : __uint_as_float(v1[i]);
+            stg[(cl + i) * 64 + f] = __float2bfloat16_rn(silu_f(g) * u);
+          }
+          named_bar_sync(2, 128);   // exchange reads and stage writes are done
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int idx = row + 128 * j;    // 16-byte piece: token idx / 8, features 8 * (idx % 8) ..
+            const int c = idx >> 3;
+            if (c0 + c < ti.rows)
+              *reinterpret_cast<uint4*>(a.out + (int64_t)(ti.row0 + c0 + c) * a.ldo + ti.fb * 64 + (idx & 7) * 8) =
+                  *reinterpret_cast<const uint4*>(stg + c * 64 + (idx & 7) * 8);
+          }
+        } else if (a.mode == kModeSwiGLU) {
           float* xb = xchg + (C::kXchgBufs == 2 ? (int)(chunk & 1u) * (64 * 33) : 0);
           const int f = q < 2 ? row : row - 64;   // feature within the tile's 64
           if (q < 2) {
@@ -620,8 +650,7 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.dest = p.dest;
   a.row_scale = p.row_scale;
   a.err = p.err;
-  a.vec_out = (p.mode != kModeSwiGLU && p.N % kBM == 0 && p.ldo % 8 == 0 &&
-               (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) ? 1 : 0;
+  a.vec_out = (p.N % kBM == 0 && p.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) ? 1 : 0;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
   // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),
