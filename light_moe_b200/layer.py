@@ -120,10 +120,10 @@ class W4A16MoELayer(torch.nn.Module):
             raise ValueError("out must be contiguous")
         y2 = out.view(-1, shape[-1])
         T = x2.shape[0]
-        device = self.gate_weight.device
-        cur = torch.cuda.current_stream(device)
         if T == 0:
             return out
+        device = self.gate_weight.device
+        cur = torch.cuda.current_stream(device)
         if chunks is None:
             chunks = min(4, T // 2560)
         n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
