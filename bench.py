@@ -176,6 +176,13 @@ def time_graph(fn, calls, replays, stream):
     return ev0.elapsed_time(ev1) / 1e3 / (calls * replays)
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the roofline
+# kernel, from ncu captures of this bench's own workloads: the gate/up GEMM at T=8192 (first
+# launch of the first layer call, 623.8 MB read + 442.0 MB written) and the decode gate/up
+# GEMM at T=64 (485.6 MB read + 7.4 MB written).  Other sizes report null.
+NCU_TRAFFIC_BYTES = {8192: 623760128 + 441977088, 64: 485.6e6 + 7.4e6}
+
+
 def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
     """Time the dominant kernel (gate/up W4A16 GEMM, SwiGLU epilogue) alone on its stream."""
     import torch
@@ -198,13 +205,15 @@ def gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind):
         return {"kernel": "grouped_gemm_kernel<192,...,W4> gate/up+SwiGLU", "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_kind} bf16 burst", "launch_us": round(secs * 1e6, 1),
-                "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
+                "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": NCU_TRAFFIC_BYTES.get(T),
+                "traffic_unit": "DRAM bytes per launch (ncu)"}
     achieved = bytes_ / secs / 1e9
     peak = peaks["hbm_gbs"]
     return {"kernel": "w4_decode_kernel gate/up+SwiGLU", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
             "peak_source": f"{peak_kind} HBM copy", "launch_us": round(secs * 1e6, 1),
-            "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": None}
+            "algorithmic": {"flops": flops, "bytes": bytes_}, "traffic": NCU_TRAFFIC_BYTES.get(T),
+            "traffic_unit": "DRAM bytes per launch (ncu)"}
 
 
 # ----------------------------------------------------------------------------- other workloads
