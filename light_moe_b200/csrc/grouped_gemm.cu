@@ -32,8 +32,12 @@
 //   last warp         the MMA issuers' waiter: waits on the stage and accumulator barriers
 //                     and publishes a counter the issuers poll
 // Every stage covers 128 K values (two 64-wide swizzle atoms), so each mbarrier wait,
-// expect-tx and commit is amortised over eight 128 x N x 16 MMAs, and the two producers
-// issue their copies in parallel.
+// expect-tx and commit is amortised over eight 128 x N x 16 MMAs per issuer.
+//
+// Epilogue: 32 accumulator columns per tensor-memory load wait; the results of each 32-column
+// step are staged token-major in shared memory and written as whole token rows (128 B for
+// SwiGLU, 256 B otherwise) with 16-byte stores; for SwiGLU the gate lanes (0-63) and up lanes
+// (64-127) exchange half of the step's columns so all four epilogue warps compute.
 //
 // Tile order: segment-major, then feature block, then token block (fastest), so the CTAs
 // working at the same time share each weight block through L2.
