@@ -100,6 +100,8 @@ def _run(world, case, timeout=120):
     # micro-batched dispatch / combine; rank 1 has fewer tokens than micro-batches
     (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[40, 1], mb=2)),
     (4, dict(E=8, S=0, k=3, d=64, F=64, g=64, T=[30, 2, 12, 25], mb=3)),
+    # fine-grained routing shape: 64 experts (16 per rank), top-6, two shared experts
+    (4, dict(E=64, S=2, k=6, d=64, F=64, g=64, T=[50, 9, 33, 20])),
 ])
 def test_expert_parallel_matches_single_process(world, case):
     results, codes = _run(world, case)
