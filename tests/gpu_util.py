@@ -80,20 +80,24 @@ def prepack(q, s, group_size, q_up=None, s_up=None):
 
 
 def w4_gemm(x, packed, N, group_size, offsets, epilogue=0, dest=None, row_scale=None, out_rows=None,
-            hint=0, seg_expert=None):
+            hint=0, seg_expert=None, pad=0):
+    """``pad`` extra output columns make the row stride ldo = ncols + pad (the returned view
+    drops them; they must stay zero)."""
     R, K = x.shape
     E = offsets.numel() - 1
     ncols = N // 2 if epilogue == 1 else N
     rows_out = out_rows if out_rows is not None else R
-    out = torch.zeros(rows_out, ncols, dtype=torch.bfloat16, device=x.device)
+    full = torch.zeros(rows_out, ncols + pad, dtype=torch.bfloat16, device=x.device)
     ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
     capi.call("lmoe_w4a16_grouped_gemm", x.data_ptr(), R, K, packed.data_ptr(), N, group_size,
               offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, capi.ptr(seg_expert), epilogue,
               capi.ptr(dest),
-              capi.ptr(row_scale), hint, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), stream())
+              capi.ptr(row_scale), hint, full.data_ptr(), ncols + pad, ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     assert read_error(ws) == 0
-    return out
+    if pad:
+        assert torch.all(full[:, ncols:] == 0), "wrote past the output columns"
+    return full[:, :ncols]
 
 
 def bf16_gemm(x, w, offsets, zero_fill=1):

@@ -146,6 +146,31 @@ def test_w4_gemm_swiglu(counts, hint):
     _assert_close(h, ref)
 
 
+@pytest.mark.parametrize("epilogue,pad", [(0, 3), (1, 5), (2, 1)])
+def test_w4_gemm_unaligned_output_stride(epilogue, pad):
+    """Row strides that are not a multiple of 8 elements take the per-element store path."""
+    counts = [200, 0, 64, 9]
+    E, F, K, g = len(counts), 256, 256, 128
+    R = sum(counts)
+    x = _w((R, K), seed=6, scale=1.0)
+    off = _offsets(counts)
+    if epilogue == 1:
+        packed, d1, d3 = _expert_setup(E, F, K, g, seed=7, paired=True)
+        h = w4_gemm(x, packed, 2 * F, g, off, epilogue=1, pad=pad)
+        _assert_close(h, torch.nn.functional.silu(_ref_plain(x, d1, off)) * _ref_plain(x, d3, off))
+        return
+    packed, deq = _expert_setup(E, F, K, g, seed=7)
+    if epilogue == 0:
+        _assert_close(w4_gemm(x, packed, F, g, off, pad=pad), _ref_plain(x, deq, off))
+        return
+    perm = torch.randperm(R + 5, device="cuda")[:R].to(torch.int32)
+    scale = torch.rand(R, device="cuda")
+    y = w4_gemm(x, packed, F, g, off, epilogue=2, dest=perm, row_scale=scale, out_rows=R + 5, pad=pad)
+    ref = torch.zeros(R + 5, F, device="cuda")
+    ref[perm.long()] = _ref_plain(x, deq, off) * scale[:, None]
+    _assert_close(y, ref)
+
+
 def test_w4_gemm_scatter():
     counts = [50, 0, 33, 77]
     E, N, K, g = 4, 256, 256, 64
