@@ -124,7 +124,38 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
   }
 }
 
-// y[t, :] = sum_{j < slots} o[t*slots + j, :]  (fp32 accumulation in slot order, bf16 out)
+// y[t, :] = sum_{j < slots} o[t*slots + j, :]  (fp32 accumulation in slot order, bf16 out);
+// 8 columns (one 16-byte load per slot row) per thread
+__global__ void combine_slots16_kernel(const uint4* __restrict__ o, int64_t T, int slots, int d8,
+                                       uint4* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * d8) return;
+  const int64_t t = i / d8;
+  const int c = (int)(i - t * d8);
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
+  const uint4* p = o + t * slots * d8 + c;
+  for (int j = 0; j < slots; ++j) {
+    const uint4 v = __ldcs(p + (int64_t)j * d8);   // read once: do not keep in L2
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+      acc[2 * q] = __fadd_rn(acc[2 * q], f.x);
+      acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], f.y);
+    }
+  }
+  uint32_t r[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+    r[q] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  y[i] = make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// the same with 2 columns per thread (outputs that are not 16-byte aligned)
 __global__ void combine_slots_kernel(const __nv_bfloat162* __restrict__ o, int64_t T, int slots, int d2,
                                      __nv_bfloat162* __restrict__ y) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -518,9 +549,15 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   if (st != LMOE_OK) return st;
   {
     const int threads = 256;
-    const int64_t n = T * (d / 2);
-    combine_slots_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
-        static_cast<const __nv_bfloat162*>(at(L.o)), T, k + S, d / 2, static_cast<__nv_bfloat162*>(y));
+    if (d % 8 == 0 && aligned16(y) && aligned16(at(L.o))) {
+      const int64_t n = T * (d / 8);
+      combine_slots16_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+          static_cast<const uint4*>(at(L.o)), T, k + S, d / 8, static_cast<uint4*>(y));
+    } else {
+      const int64_t n = T * (d / 2);
+      combine_slots_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+          static_cast<const __nv_bfloat162*>(at(L.o)), T, k + S, d / 2, static_cast<__nv_bfloat162*>(y));
+    }
     LMOE_CUDA_TRY(cudaGetLastError());
   }
   return LMOE_OK;
