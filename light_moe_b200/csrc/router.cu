@@ -14,7 +14,7 @@
 // after two dtype-conversion copies, a CUDA-core softmax/top-k kernel for E in {8,16} and
 // top-2 only, and ~2E+6 ATen launches for counts/offsets/argsort; here it is one kernel.
 //
-// Structure (persistent, one CTA per SM, up to 128 tokens per tile, 11 warps):
+// Structure (persistent, one CTA per SM, up to 128 tokens per tile, 10 warps):
 //   warp 0     TMA producer: two x tiles [128 x 64] and two W tiles [Epad x 64] per stage
 //              (128B swizzle; 256 contiguous bytes of every token row per stage)
 //   warp 1     MMA issuer: 8 x tcgen05.mma (M=128, N=Epad, K=16) per stage into one of two
@@ -23,8 +23,6 @@
 //              per-tile expert bitmap for the permutation
 //   warps 6-9  epilogue helpers (more than 16 experts): the upper half of each row's expert
 //              columns (exponentials, partial top-k), exchanged through shared memory
-//   warp 10    waits on the stage and accumulator barriers for the MMA issuer and publishes
-//              a counter it polls
 // When the permutation is requested the kernel is launched cooperatively and, after a grid
 // barrier, every CTA scans the per-tile counts and scatters its tokens into sorted_idx.
 #include <cuda_bf16.h>
@@ -42,8 +40,7 @@ constexpr int kBM = 128;          // MMA rows per tile; a tile holds bm <= kBM t
 constexpr int kBK = 64;           // hidden elements per TMA box (one 128-byte swizzle row)
 constexpr int kBoxes = 2;         // boxes per pipeline stage: 128 hidden elements per stage
 constexpr int kEpiWarps = 4;      // epilogue warps that own the token rows (one per TMEM lane quarter)
-constexpr int kWaitWarp = 2 + 2 * kEpiWarps;     // waits on the stage barriers for the MMA issuer
-constexpr int kThreads = 32 * (kWaitWarp + 1);   // producer, MMA issuer, owners, helpers, waiter: 11 warps
+constexpr int kThreads = 64 + 2 * 32 * kEpiWarps;   // producer, MMA issuer, owners, helpers: 10 warps
 constexpr uint32_t kEpiAllBar = 6;   // named barrier of all epilogue threads (ids 1-5: owners, pairs)
 constexpr int kMaxStages = 8;
 constexpr int kMaxExperts = 256;
@@ -77,7 +74,6 @@ struct __align__(8) RouterHdr {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t mma_done;
-  uint32_t ready;         // stages published to the MMA issuer by the waiter warp
   uint32_t tmem_base;
   int abort;
   float bias[kMaxExperts];
@@ -127,7 +123,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&h->acc_empty[b], 128);
     }
     mbar_init(&h->mma_done, 1);
-    h->ready = 0;
     h->abort = 0;
     fence_mbar_init();
   }
@@ -184,12 +179,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++lt) {
         const uint32_t acc = lt & 1u;
+        if (!mbar_wait(&h->acc_empty[acc], ((lt >> 1) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)) break;
+        tc_fence_after();
         const uint32_t d_tmem = tmem + acc * a.Epad;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % a.stages;
-          // published by the waiter warp once the stage has landed (and, at a tile start, the
-          // accumulator is free): an mbarrier wait here would cost ~270 cycles per stage
-          if (!counter_wait(&h->ready, it, a.err, abort_flag, kSite + 4)) { ok = false; break; }
+          if (!mbar_wait(&h->full[s], (it / a.stages) & 1u, a.err, abort_flag, kSite + 4)) { ok = false; break; }
           tc_fence_after();
           const uint32_t xa = smem_u32(base + s * a.stage_bytes);
           const uint32_t wa = xa + kBoxes * kXBox;
@@ -211,25 +206,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // all issued MMAs must retire before the tensor memory is released
       mma_commit(&h->mma_done);
       mbar_wait(&h->mma_done, 0, a.err, nullptr, kSite + 5);
-    }
-  } else if (warp == kWaitWarp) {
-    // ------------------------------------------------------------------ MMA issuer's waiter
-    // Parity waits stay exact: the stage barrier of round r + 1 needs the issuer's commit of
-    // round r, which needs this warp's publication of round r.
-    if (lane == 0) {
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++lt) {
-        const uint32_t acc = lt & 1u;
-        if (!mbar_wait(&h->acc_empty[acc], ((lt >> 1) & 1u) ^ 1u, a.err, abort_flag, kSite + 3)) break;
-        for (int kc = 0; kc < nk; ++kc, ++it) {
-          if (!mbar_wait(&h->full[it % a.stages], (it / a.stages) & 1u, a.err, abort_flag, kSite + 8)) {
-            ok = false;
-            break;
-          }
-          st_release_shared(&h->ready, it + 1);
-        }
-      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue
