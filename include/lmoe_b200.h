@@ -29,6 +29,11 @@ extern "C" {
 #define LMOE_ERR_WORKSPACE (-3)      /* workspace missing or too small                    */
 #define LMOE_ERR_DEVICE (-4)         /* current device is not sm_100 / kernel error word  */
 
+/* Element types of floating-point operands (the *_typed entry points). */
+#define LMOE_DTYPE_BF16 0
+#define LMOE_DTYPE_F16 1
+#define LMOE_DTYPE_F32 2
+
 typedef struct CUstream_st* lmoe_stream_t; /* identical to cudaStream_t */
 
 /* Library version as 10000*major + 100*minor + patch. */
@@ -77,6 +82,23 @@ int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const floa
                          int32_t* positions, float* logits,
                          void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
 
+/* lmoe_fused_gate_topk for hidden states and gate weight of any of the LMOE_DTYPE_* types
+ * (x_dtype, w_dtype), as the reference's binding accepts any floating dtype and computes the
+ * logits in fp32 from the converted operands (csrc/fused_moe_ops.cu:158-159):
+ *   - both bf16 or both fp16: tensor-core logits (16-bit products are exact in fp32, fp32
+ *     accumulation);
+ *   - otherwise (fp32 on either side, or bf16 with fp16): fp32 logits on CUDA cores from the
+ *     caller's values, each a sequential fp32 sum over the hidden dimension.
+ * Workspace: lmoe_router_workspace_bytes_typed().  Everything else as lmoe_fused_gate_topk. */
+size_t lmoe_router_workspace_bytes_typed(int64_t num_tokens, int num_experts, int x_dtype, int w_dtype);
+
+int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const void* gate_weight, int w_dtype,
+                               const float* gate_bias, int64_t num_tokens, int hidden_size, int num_experts,
+                               int top_k, int32_t* ids, float* weights, void* weights_bf16,
+                               int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
+                               int32_t* positions, float* logits,
+                               void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
+
 /* lmoe_fused_gate_topk without a workspace argument (no counterpart in the reference): the
  * scratch lives in a fixed 1.25 MB device array inside this library, for callers that may
  * not allocate device memory (an allocator that owns all device memory, a serving loop that
@@ -100,12 +122,13 @@ int lmoe_fused_gate_topk_static(const void* hidden, const void* gate_weight, con
 /* Row gather / weighted combine                                                          */
 /* ------------------------------------------------------------------------------------ */
 
-/* permuted[r, :] = hidden[sorted_idx[r] / top_k, :] for r < rows (bf16, hidden % 8 == 0).
+/* permuted[r, :] = hidden[sorted_idx[r] / top_k, :] for r < rows; elements of elem_bytes
+ * (2 or 4) bytes, hidden_size * elem_bytes a multiple of 16, rows copied unchanged.
  * Replaces the expand + index_select of fused_gate_topk_permute_cuda
  * (csrc/fused_moe_ops.cu:227-228) and permute_tokens (python/light_moe/ops/grouped_gemm.py:
  * 202-247). */
-int lmoe_permute_rows(const void* hidden, const int32_t* sorted_idx, int64_t rows, int hidden_size,
-                      int top_k, void* permuted, lmoe_stream_t stream);
+int lmoe_permute_rows(const void* hidden, int elem_bytes, const int32_t* sorted_idx, int64_t rows,
+                      int hidden_size, int top_k, void* permuted, lmoe_stream_t stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* int4 weight format (defined by this library; the reference only has the unused flag    */
@@ -146,10 +169,20 @@ int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_a,
 
 size_t lmoe_gemm_workspace_bytes(void);
 
-/* Dense bf16 weights [num_experts, N, K].  output bf16 [total_rows, N]; with zero_fill the
- * rows outside every expert range are zeroed first.
+/* Dense weights [num_experts, N, K] of the input's type.  output [total_rows, N] of the
+ * same type; with zero_fill the rows outside every expert range are zeroed first.
+ * dtype LMOE_DTYPE_BF16 / LMOE_DTYPE_F16: tcgen05 tensor cores (exact 16-bit products, fp32
+ * accumulation, K % 64 == 0); LMOE_DTYPE_F32: fp32 FFMA on CUDA cores (K % 4 == 0), as the
+ * reference's fp32 cuBLAS GEMM computes in fp32.
  * Replaces grouped_gemm_cuda (csrc/grouped_gemm.cu:11-43), which zero-fills (:24), copies
- * the offsets to the host (:27) and runs one cuBLAS GEMM per expert (:30-40). */
+ * the offsets to the host (:27) and runs one cuBLAS GEMM per expert in the input dtype
+ * (:30-40). */
+int lmoe_grouped_gemm(const void* input, int dtype, int64_t total_rows, int K, const void* weights, int N,
+                      const void* expert_offsets, int offsets_are_int64, int num_experts,
+                      int zero_fill, void* output, void* workspace, size_t workspace_bytes,
+                      lmoe_stream_t stream);
+
+/* lmoe_grouped_gemm with dtype LMOE_DTYPE_BF16. */
 int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const void* weights, int N,
                            const void* expert_offsets, int offsets_are_int64, int num_experts,
                            int zero_fill, void* output, void* workspace, size_t workspace_bytes,
@@ -163,6 +196,11 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
  * epilogue 2: output[dest_rows[r], n] = row_scale[r] * acc       (NULL = identity / 1)
  * segment_expert: weight matrix used by each of the num_experts row segments (NULL: the
  *             identity), so rows grouped by (source, expert) need no re-sort.
+ * num_weight_matrices: matrices held by `packed`; every segment_expert entry (or, without a
+ *             map, every segment index) must lie in [0, num_weight_matrices).  A kernel that
+ *             finds an entry outside it, or offsets that decrease or pass total_rows, skips
+ *             that segment and writes a nonzero error word into the workspace
+ *             (lmoe_read_error).
  * max_rows_per_expert: an upper bound of any expert's row count if known (0 = unknown);
  * small bounds select the decode-sized tiles.
  * New op; the reference has no W4A16 GEMM (SparseMoEBlockFast's GroupedLinear calls,
@@ -170,7 +208,7 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
 int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed,
                             int N, int group_size,
                             const void* expert_offsets, int offsets_are_int64, int num_experts,
-                            const int32_t* segment_expert,
+                            const int32_t* segment_expert, int num_weight_matrices,
                             int epilogue, const int32_t* dest_rows, const float* row_scale,
                             int64_t max_rows_per_expert, void* output, int64_t ldo,
                             void* workspace, size_t workspace_bytes, lmoe_stream_t stream);

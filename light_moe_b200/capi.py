@@ -19,6 +19,10 @@ LMOE_ERR_UNSUPPORTED = -2
 LMOE_ERR_WORKSPACE = -3
 LMOE_ERR_DEVICE = -4
 
+LMOE_DTYPE_BF16 = 0
+LMOE_DTYPE_F16 = 1
+LMOE_DTYPE_F32 = 2
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _I64 = ctypes.c_int64
@@ -30,16 +34,20 @@ SIGNATURES = {
     "lmoe_status_string": (ctypes.c_char_p, [_I]),
     "lmoe_read_error": (_I, [_P, _P, _P]),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
+    "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),
+    "lmoe_fused_gate_topk_typed": (_I, [_P, _I, _P, _I, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                        _SZ, _P]),
     "lmoe_fused_gate_topk": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "lmoe_fused_gate_topk_static": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
-    "lmoe_permute_rows": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
+    "lmoe_permute_rows": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P]),
     "lmoe_quantize_w4": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P]),
     "lmoe_dequantize_w4": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "lmoe_w4_prepacked_bytes": (_I, [_I, _I, _I, _I, _I, _P]),
     "lmoe_prepack_w4": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "lmoe_gemm_workspace_bytes": (_SZ, []),
+    "lmoe_grouped_gemm": (_I, [_P, _I, _I64, _I, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "lmoe_grouped_gemm_bf16": (_I, [_P, _I64, _I, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
-    "lmoe_w4a16_grouped_gemm": (_I, [_P, _I64, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _P, _I64, _P, _I64, _P,
+    "lmoe_w4a16_grouped_gemm": (_I, [_P, _I64, _I, _P, _I, _I, _P, _I, _I, _P, _I, _I, _P, _P, _I64, _P, _I64, _P,
                                      _SZ, _P]),
     "lmoe_combine_rows": (_I, [_P, _P, _P, _I64, _I, _I, _P, _I, _P, _P]),
     "lmoe_moe_layer_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I]),
@@ -85,6 +93,16 @@ def call(name: str, *args) -> None:
 def ptr(t) -> int | None:
     """Device pointer of a torch tensor (None for None)."""
     return None if t is None else t.data_ptr()
+
+
+def dtype_code(dtype) -> int:
+    """LMOE_DTYPE_* code of a torch floating dtype (bf16, fp16, fp32)."""
+    import torch
+
+    codes = {torch.bfloat16: LMOE_DTYPE_BF16, torch.float16: LMOE_DTYPE_F16, torch.float32: LMOE_DTYPE_F32}
+    if dtype not in codes:
+        raise ValueError(f"unsupported dtype {dtype}")
+    return codes[dtype]
 
 
 def stream_handle(stream=None) -> int:

@@ -28,6 +28,25 @@ torch::Tensor as_bf16_contig(const torch::Tensor& t) {
   return t.scalar_type() == torch::kBFloat16 ? t.contiguous() : t.to(torch::kBFloat16).contiguous();
 }
 
+// The operand as one of the library's element types: bf16, fp16 and fp32 pass unchanged;
+// any other floating type becomes fp32, the type the reference converts every operand to
+// (csrc/fused_moe_ops.cu:158-159).
+torch::Tensor as_kernel_type(const torch::Tensor& t) {
+  const auto st = t.scalar_type();
+  if (st == torch::kBFloat16 || st == torch::kFloat16 || st == torch::kFloat32) return t.contiguous();
+  return t.to(torch::kFloat32).contiguous();
+}
+
+int dtype_code(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kBFloat16: return LMOE_DTYPE_BF16;
+    case torch::kFloat16: return LMOE_DTYPE_F16;
+    case torch::kFloat32: return LMOE_DTYPE_F32;
+    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+  }
+  return -1;
+}
+
 void check_cuda(const torch::Tensor& t, const char* name) { TORCH_CHECK(t.is_cuda(), name, " must be CUDA"); }
 
 torch::Tensor workspace(int64_t bytes, const torch::Tensor& like) {
@@ -45,8 +64,8 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
   TORCH_CHECK(hidden_states.dim() == 2 && gate_weight.dim() == 2, "hidden_states [T,d] and gate_weight [E,d]");
   TORCH_CHECK(hidden_states.size(1) == gate_weight.size(1), "hidden size mismatch");
   const c10::cuda::OptionalCUDAGuard guard(hidden_states.device());
-  auto x = as_bf16_contig(hidden_states);
-  auto w = as_bf16_contig(gate_weight);
+  auto x = as_kernel_type(hidden_states);
+  auto w = as_kernel_type(gate_weight);
   const int64_t T = x.size(0);
   const int64_t d = x.size(1);
   const int64_t E = w.size(0);
@@ -67,8 +86,10 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
     r.positions = torch::empty({T * top_k}, i32);
   }
   if (want_logits) r.logits = torch::empty({T, E}, x.options().dtype(torch::kFloat32));
-  auto ws = workspace((int64_t)lmoe_router_workspace_bytes(T, (int)E), x);
-  int st = lmoe_fused_gate_topk(x.data_ptr(), w.data_ptr(), b.defined() ? b.data_ptr<float>() : nullptr, T, (int)d,
+  const int xdt = dtype_code(x), wdt = dtype_code(w);
+  auto ws = workspace((int64_t)lmoe_router_workspace_bytes_typed(T, (int)E, xdt, wdt), x);
+  int st = lmoe_fused_gate_topk_typed(x.data_ptr(), xdt, w.data_ptr(), wdt, b.defined() ? b.data_ptr<float>() : nullptr,
+                                T, (int)d,
                                 (int)E, (int)top_k, r.ids.data_ptr<int32_t>(), r.weights.data_ptr<float>(), nullptr,
                                 perm ? r.counts.data_ptr<int32_t>() : nullptr,
                                 perm ? r.offsets.data_ptr<int32_t>() : nullptr,
@@ -94,14 +115,22 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Te
     torch::Tensor hidden_states, torch::Tensor gate_weight, int64_t top_k) {
   Routed r = route(hidden_states, gate_weight, std::nullopt, top_k, true, false);
   const c10::cuda::OptionalCUDAGuard guard(hidden_states.device());
-  auto x = as_bf16_contig(hidden_states);
+  // the permuted rows are the caller's rows, copied unchanged in their own dtype
+  auto x = hidden_states.contiguous();
   const int64_t T = x.size(0);
   const int64_t d = x.size(1);
   auto permuted = torch::empty({T * top_k, d}, x.options());
-  int st = lmoe_permute_rows(x.data_ptr(), r.sorted_idx.data_ptr<int32_t>(), T * top_k, (int)d, (int)top_k,
-                             permuted.data_ptr(), cur_stream());
+  const int esize = (int)x.element_size();
+  int st = LMOE_OK;
+  if ((esize == 2 || esize == 4) && (d * esize) % 16 == 0) {
+    st = lmoe_permute_rows(x.data_ptr(), esize, r.sorted_idx.data_ptr<int32_t>(), T * top_k, (int)d, (int)top_k,
+                           permuted.data_ptr(), cur_stream());
+  } else {
+    // other element sizes or row lengths: the same gather through ATen
+    permuted = x.index_select(0, r.sorted_idx.to(torch::kInt64).floor_divide(top_k));
+  }
   check_status(st, "fused_gate_topk_permute");
-  return {permuted.to(hidden_states.scalar_type()), r.ids, r.weights.to(hidden_states.scalar_type()),
+  return {permuted, r.ids, r.weights.to(hidden_states.scalar_type()),
           r.offsets.to(torch::kInt64), r.sorted_idx.to(torch::kInt64)};
 }
 
@@ -115,16 +144,18 @@ torch::Tensor grouped_gemm(torch::Tensor input, torch::Tensor weights, torch::Te
   TORCH_CHECK(weights.size(0) >= num_experts && weights.size(2) == input.size(1), "shape mismatch");
   TORCH_CHECK(expert_offsets.numel() >= num_experts + 1, "expert_offsets must have num_experts + 1 entries");
   const c10::cuda::OptionalCUDAGuard guard(input.device());
-  auto x = as_bf16_contig(input);
-  auto w = as_bf16_contig(weights);
+  // computed in the input dtype (bf16 / fp16 on tensor cores, fp32 on CUDA cores), like the
+  // reference's per-expert mm_out (csrc/grouped_gemm.cu:24-40); the weights follow the input
+  auto x = as_kernel_type(input);
+  auto w = weights.scalar_type() == x.scalar_type() ? weights.contiguous() : weights.to(x.scalar_type()).contiguous();
   auto off = expert_offsets.contiguous();
   TORCH_CHECK(off.scalar_type() == torch::kInt64 || off.scalar_type() == torch::kInt32, "offsets int64/int32");
   const int64_t T = x.size(0), K = x.size(1), N = w.size(1);
   auto out = torch::empty({T, N}, x.options());
   auto ws = workspace((int64_t)lmoe_gemm_workspace_bytes(), x);
-  int st = lmoe_grouped_gemm_bf16(x.data_ptr(), T, (int)K, w.data_ptr(), (int)N, off.data_ptr(),
-                                  off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts, 1, out.data_ptr(),
-                                  ws.data_ptr(), ws.numel(), cur_stream());
+  int st = lmoe_grouped_gemm(x.data_ptr(), dtype_code(x), T, (int)K, w.data_ptr(), (int)N, off.data_ptr(),
+                             off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts, 1, out.data_ptr(),
+                             ws.data_ptr(), ws.numel(), cur_stream());
   check_status(st, "grouped_gemm");
   return out.to(input.scalar_type());
 }
@@ -223,10 +254,15 @@ torch::Tensor w4a16_grouped_gemm(torch::Tensor input, torch::Tensor packed, torc
   if (row_scale.has_value() && row_scale->defined()) rs = row_scale->to(torch::kFloat32).contiguous();
   torch::Tensor se;
   if (segment_expert.has_value() && segment_expert->defined()) se = segment_expert->to(torch::kInt32).contiguous();
+  // weight matrices held by `packed` (each N x K in the prepacked layout)
+  size_t per = 0;
+  check_status(lmoe_w4_prepacked_bytes(1, (int)N, (int)K, (int)group_size, 0, &per), "w4a16_grouped_gemm");
+  TORCH_CHECK(per > 0 && packed.numel() % (int64_t)per == 0, "packed size is not a whole number of matrices");
+  const int num_w = (int)(packed.numel() / (int64_t)per);
   auto ws = workspace((int64_t)lmoe_gemm_workspace_bytes(), x);
   int st = lmoe_w4a16_grouped_gemm(
       x.data_ptr(), T, (int)K, packed.data_ptr<uint8_t>(), (int)N, (int)group_size, off.data_ptr(), off.scalar_type() == torch::kInt64 ? 1 : 0, (int)num_experts,
-      se.defined() ? se.data_ptr<int32_t>() : nullptr, (int)epilogue, dr.defined() ? dr.data_ptr<int32_t>() : nullptr, rs.defined() ? rs.data_ptr<float>() : nullptr,
+      se.defined() ? se.data_ptr<int32_t>() : nullptr, num_w, (int)epilogue, dr.defined() ? dr.data_ptr<int32_t>() : nullptr, rs.defined() ? rs.data_ptr<float>() : nullptr,
       max_rows_per_expert, out.data_ptr(), ncols, ws.data_ptr(), ws.numel(), cur_stream());
   check_status(st, "w4a16_grouped_gemm");
   return out;

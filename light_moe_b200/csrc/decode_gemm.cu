@@ -2,8 +2,10 @@
 //
 // Same inputs as grouped_gemm.cu: segments of rows of X (bf16 [R, K]), the prepacked int4
 // super-blocks (w4_layout.cuh, scales embedded) -- one weight copy serves both kernels.
-// Reference semantics: csrc/grouped_gemm.cu:11-43 applied to the dequantised weights of
-// python/light_moe/model/quantized_experts.py (w = q * s per group of K values).
+// Reference semantics: csrc/grouped_gemm.cu:11-43 (one GEMM per expert segment) applied to
+// the dequantised int4 weights (w = q * s per group of K values; the int4 format itself is
+// defined by this library, the reference only has the unused flag
+// python/light_moe/engine/executor.py:44-48).
 //
 // Why a second kernel.  With a handful of tokens per expert the GEMM is a weight stream:
 // 8.5 KB of int4 per 128 x 128 super-block, ~23 bytes per SM per cycle at HBM speed, i.e.
@@ -97,6 +99,7 @@ struct DecodeArgs {
   void* out;          // bf16 (plain / SwiGLU) or fp32 [ksplit][R][N] (partials)
   int64_t ldo;
   int64_t R;
+  int num_w;          // weight matrices available
   uint32_t* err;
 };
 
@@ -206,8 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   for (int e = tid; e <= a.E; e += kThreads) {
-    bars->row_off[e] = a.offsets_i64 ? (int)static_cast<const int64_t*>(a.offsets)[e]
-                                     : static_cast<const int32_t*>(a.offsets)[e];
+    const int64_t o = a.offsets_i64 ? static_cast<const int64_t*>(a.offsets)[e]
+                                    : (int64_t) static_cast<const int32_t*>(a.offsets)[e];
+    bars->row_off[e] = (int)(o < 0 ? -1 : (o > a.R ? a.R + 1 : o));   // out of range -> caught below
     if (e < a.E) bars->seg_w[e] = a.seg_expert ? a.seg_expert[e] : e;
   }
   __syncthreads();
@@ -216,8 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->tile_start[0] = 0;
     for (int e = 0; e < a.E; ++e) {
       int n_e = bars->row_off[e + 1] - bars->row_off[e];
-      if (n_e < 0) {
-        report_error(a.err, kErrBadArg, kSite + 9);
+      // a segment whose rows or weight matrix lie outside the buffers is skipped
+      if (n_e < 0 || bars->row_off[e] < 0 || bars->row_off[e + 1] > a.R || bars->seg_w[e] < 0 ||
+          bars->seg_w[e] >= a.num_w) {
+        if (n_e != 0) report_error(a.err, kErrBadArg, kSite + 9);
         n_e = 0;
       }
       acc_t += ((n_e + kBN - 1) / kBN) * a.NB * a.ksplit;
@@ -496,6 +502,7 @@ int run_decode_gemm(const DecodeProblem& p, cudaStream_t stream) {
   a.out = p.out;
   a.ldo = p.ldo;
   a.R = p.total_rows;
+  a.num_w = p.num_w > 0 ? p.num_w : p.num_experts;
   a.err = p.err;
   CUtensorMap tm_x16, tm_x32;
   st = encode_tmap_2d(&tm_x16, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,

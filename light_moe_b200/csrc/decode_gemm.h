@@ -23,6 +23,7 @@ struct DecodeProblem {
   int offsets_i64 = 0;
   int num_experts = 0;
   const int32_t* seg_expert = nullptr;
+  int num_w = 0;                // weight matrices available (segments mapping outside are skipped)
   const uint8_t* wq = nullptr;  // prepacked super-blocks
   int group_size = 0;
   int N = 0;                    // weight rows per matrix (multiple of 128)

@@ -47,6 +47,7 @@
 //   kSwiGLU  out[r, fb*64 + j]  (tile rows j: gate, j+64: up) = bf16(silu(gate) * up)
 //   kScatter out[dest[r], n]                                  = bf16(scale[r] * acc)
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "grouped_gemm.h"
 #include "host_util.h"
@@ -78,7 +79,15 @@ struct GemmArgs {
   uint32_t* err;
   uint32_t tmem_cols;
   int vec_out;                // N % 128 == 0, ldo % 8 == 0, out 16-byte aligned: staged 16-byte stores
+  int ab_f16;                 // dense operands fp16 (else bf16); plain outputs written as fp16
+  int num_w;                  // weight matrices available
+  int64_t R;                  // activation rows
 };
+
+// fp32 -> the 16-bit output type (bf16, or fp16 for fp16 operands), as bf16 storage.
+__device__ __forceinline__ __nv_bfloat16 cvt_out(float v, int f16) {
+  return f16 ? __ushort_as_bfloat16(__half_as_ushort(__float2half_rn(v))) : __float2bfloat16_rn(v);
+}
 
 constexpr int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
 constexpr int lcm_int(int a, int b) { return a / gcd_int(a, b) * b; }
@@ -208,8 +217,9 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
   }
   // segment row offsets, weight map and the tile prefix (computed redundantly by every CTA)
   for (int e = tid; e <= a.E; e += C::kThreads) {
-    bars->row_off[e] = a.offsets_i64 ? (int)static_cast<const int64_t*>(a.offsets)[e]
-                                     : static_cast<const int32_t*>(a.offsets)[e];
+    const int64_t o = a.offsets_i64 ? static_cast<const int64_t*>(a.offsets)[e]
+                                    : (int64_t) static_cast<const int32_t*>(a.offsets)[e];
+    bars->row_off[e] = (int)(o < 0 ? -1 : (o > a.R ? a.R + 1 : o));   // out of range -> caught below
     if (e < a.E) bars->seg_w[e] = a.seg_expert ? a.seg_expert[e] : e;
   }
   __syncthreads();
@@ -218,8 +228,10 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
     bars->tile_start[0] = 0;
     for (int e = 0; e < a.E; ++e) {
       int n_e = bars->row_off[e + 1] - bars->row_off[e];
-      if (n_e < 0) {
-        report_error(a.err, kErrBadArg, kSite + 9);
+      // a segment whose rows or weight matrix lie outside the buffers is skipped
+      if (n_e < 0 || bars->row_off[e] < 0 || bars->row_off[e + 1] > a.R || bars->seg_w[e] < 0 ||
+          bars->seg_w[e] >= a.num_w) {
+        if (n_e != 0) report_error(a.err, kErrBadArg, kSite + 9);
         n_e = 0;
       }
       acc_t += ((n_e + BN - 1) / BN) * a.NB;
@@ -315,7 +327,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
         const int n_eff = (ti.rows + 15) & ~15;
         int n_mine = n_eff - half * (BN / 2);   // this issuer's columns, a multiple of 16
         n_mine = n_mine < 0 ? 0 : (n_mine > BN / 2 ? BN / 2 : n_mine);
-        const uint32_t idesc = idesc_bf16_f32(kBM, n_mine > 0 ? (uint32_t)n_mine : 16u);
+        const uint32_t idesc = idesc_f16kind_f32(kBM, n_mine > 0 ? (uint32_t)n_mine : 16u, a.ab_f16);
         const uint32_t acc = lt % ACC;
         const uint32_t d_tmem = tmem + acc * BN + half * (BN / 2);
         for (int ks = 0; ks < KS; ++ks, ++it) {
@@ -546,7 +558,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
               const int c = 16 * h + i;
               float val = __uint_as_float(h ? v1[i] : v0[i]);
               if (a.mode == kModeScatter && a.row_scale && c0 + c < ti.rows) val = __fmul_rn(val, tscale[c0 + c]);
-              stg[c * kBM + row] = __float2bfloat16_rn(val);
+              stg[c * kBM + row] = cvt_out(val, a.ab_f16);
             }
           }
           named_bar_sync(2, 128);
@@ -574,7 +586,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
                   if (a.row_scale) val = __fmul_rn(val, tscale[c]);
                   orow = tdest[c];
                 }
-                a.out[orow * a.ldo + feat] = __float2bfloat16_rn(val);
+                a.out[orow * a.ldo + feat] = cvt_out(val, a.ab_f16);
               }
             }
           }
@@ -655,18 +667,22 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.row_scale = p.row_scale;
   a.err = p.err;
   a.vec_out = (p.N % kBM == 0 && p.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) ? 1 : 0;
+  a.ab_f16 = (!w4 && p.ab_f16) ? 1 : 0;
+  a.num_w = p.num_w > 0 ? p.num_w : p.num_experts;
+  a.R = p.total_rows;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
   // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),
   // the whole 192-row tile otherwise
   const int box = small ? 16 : 192;
+  const CUtensorMapDataType tdt = a.ab_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tm_x, tm_w;
-  st = encode_tmap_2d(&tm_x, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,
-                      (uint64_t)p.ldx * 2, (uint32_t)box, kBK, true);
+  st = encode_tmap_2d(&tm_x, p.x, tdt, 2, (uint64_t)p.total_rows, (uint64_t)p.K, (uint64_t)p.ldx * 2, (uint32_t)box,
+                      kBK, true);
   if (st != LMOE_OK) return st;
   if (!w4) {
-    st = encode_tmap_2d(&tm_w, p.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.num_experts * p.N,
-                        (uint64_t)p.K, (uint64_t)p.K * 2, kBM, kBK, true);
+    st = encode_tmap_2d(&tm_w, p.w, tdt, 2, (uint64_t)a.num_w * p.N, (uint64_t)p.K, (uint64_t)p.K * 2, kBM, kBK,
+                        true);
     if (st != LMOE_OK) return st;
   } else {
     tm_w = tm_x;

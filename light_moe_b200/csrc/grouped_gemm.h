@@ -27,10 +27,12 @@ struct GemmProblem {
   // weight matrix of each segment (NULL: segment e uses matrix e); lets rows that arrive
   // grouped by (source rank, expert) be multiplied without a local re-sort
   const int32_t* seg_expert = nullptr;
+  int num_w = 0;        // weight matrices available; segments mapping outside [0, num_w) are skipped
   // weights: either W4 prepacked super-blocks (wq, scales embedded) or bf16 [num_experts, N, K] (w)
   const uint8_t* wq = nullptr;
   int group_size = 0;
   const void* w = nullptr;
+  int ab_f16 = 0;       // dense weights and activations are fp16 (else bf16); output of the same type
   int N = 0;  // weight rows per expert (for SwiGLU: 2 * features)
   // epilogue
   int mode = kModePlain;
@@ -44,5 +46,10 @@ struct GemmProblem {
 };
 
 int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream);
+
+// Dense fp32 grouped GEMM on CUDA cores (fp32 FFMA): out[r, n] = sum_k x[r, k] * w[e, n, k]
+// for the rows r of segment e; K % 4 == 0, x / w / out 16-byte aligned.
+int run_grouped_gemm_f32(const float* x, int64_t total_rows, int K, const float* w, int N, const void* offsets,
+                         int offsets_i64, int num_experts, float* out, uint32_t* err, cudaStream_t stream);
 
 }  // namespace lmoe

@@ -13,7 +13,35 @@ DeviceInfo g_info[kMaxDevices];
 std::mutex g_info_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
 }  // namespace
+
+int current_context_id(unsigned long long* id) {
+  std::call_once(g_ctx_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  if (!g_ctx_current || !g_ctx_id) return LMOE_ERR_DEVICE;
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS) return LMOE_ERR_DEVICE;
+  if (!ctx) {   // no context bound to this thread yet
+    *id = 0;
+    return LMOE_OK;
+  }
+  unsigned long long v = 0;
+  if (g_ctx_id(ctx, &v) != CUDA_SUCCESS) return LMOE_ERR_DEVICE;
+  *id = v;
+  return LMOE_OK;
+}
 
 int get_device_info(DeviceInfo* out) {
   int dev = 0;

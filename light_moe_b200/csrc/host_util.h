@@ -37,6 +37,10 @@ struct DeviceInfo {
 
 int get_device_info(DeviceInfo* out);
 
+// Process-unique id of the calling thread's current CUDA context (cuCtxGetId); 0 when no
+// context is bound to the thread yet.
+int current_context_id(unsigned long long* id);
+
 // cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, smem) on the current device, skipped
 // when this (kernel, device) already allows at least `smem` bytes: the attribute call costs
 // microseconds of host time on every launch otherwise.

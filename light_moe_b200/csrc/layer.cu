@@ -314,18 +314,24 @@ extern "C" int lmoe_prepack_w4(const uint8_t* qweight_a, const uint16_t* scales_
 
 extern "C" size_t lmoe_gemm_workspace_bytes(void) { return 256; }
 
-extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const void* weights, int N,
-                                      const void* expert_offsets, int offsets_are_int64, int num_experts,
-                                      int zero_fill, void* output, void* workspace, size_t workspace_bytes,
-                                      lmoe_stream_t stream_) {
+extern "C" int lmoe_grouped_gemm(const void* input, int dtype, int64_t total_rows, int K, const void* weights, int N,
+                                 const void* expert_offsets, int offsets_are_int64, int num_experts, int zero_fill,
+                                 void* output, void* workspace, size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(dtype == LMOE_DTYPE_BF16 || dtype == LMOE_DTYPE_F16 || dtype == LMOE_DTYPE_F32);
   LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1);
   LMOE_ARG_CHECK(input && weights && expert_offsets && output);
-  LMOE_ARG_CHECK(aligned16(input) && aligned16(weights) && K % 64 == 0);
+  LMOE_ARG_CHECK(aligned16(input) && aligned16(weights));
+  LMOE_ARG_CHECK(dtype == LMOE_DTYPE_F32 ? (K % 4 == 0) : (K % 64 == 0));
   if (!workspace || workspace_bytes < 256) return LMOE_ERR_WORKSPACE;
+  const size_t esize = dtype == LMOE_DTYPE_F32 ? 4 : 2;
   if (zero_fill && total_rows > 0)
-    LMOE_CUDA_TRY(cudaMemsetAsync(output, 0, (size_t)total_rows * N * sizeof(uint16_t), stream));
+    LMOE_CUDA_TRY(cudaMemsetAsync(output, 0, (size_t)total_rows * N * esize, stream));
   LMOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, 256, stream));
+  if (dtype == LMOE_DTYPE_F32)
+    return run_grouped_gemm_f32(static_cast<const float*>(input), total_rows, K, static_cast<const float*>(weights),
+                                N, expert_offsets, offsets_are_int64, num_experts, static_cast<float*>(output),
+                                static_cast<uint32_t*>(workspace), stream);
   GemmProblem p;
   p.x = input;
   p.ldx = K;
@@ -334,7 +340,9 @@ extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int
   p.offsets = expert_offsets;
   p.offsets_i64 = offsets_are_int64;
   p.num_experts = num_experts;
+  p.num_w = num_experts;
   p.w = weights;
+  p.ab_f16 = dtype == LMOE_DTYPE_F16 ? 1 : 0;
   p.N = N;
   p.mode = kModePlain;
   p.out = output;
@@ -343,15 +351,25 @@ extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int
   return run_grouped_gemm(p, stream);
 }
 
+extern "C" int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const void* weights, int N,
+                                      const void* expert_offsets, int offsets_are_int64, int num_experts,
+                                      int zero_fill, void* output, void* workspace, size_t workspace_bytes,
+                                      lmoe_stream_t stream) {
+  return lmoe_grouped_gemm(input, LMOE_DTYPE_BF16, total_rows, K, weights, N, expert_offsets, offsets_are_int64,
+                           num_experts, zero_fill, output, workspace, workspace_bytes, stream);
+}
+
 extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const uint8_t* packed, int N,
                                        int group_size,
                                        const void* expert_offsets, int offsets_are_int64, int num_experts,
-                                       const int32_t* segment_expert, int epilogue, const int32_t* dest_rows,
+                                       const int32_t* segment_expert, int num_weight_matrices, int epilogue,
+                                       const int32_t* dest_rows,
                                        const float* row_scale,
                                        int64_t max_rows_per_expert, void* output, int64_t ldo, void* workspace,
                                        size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1);
+  LMOE_ARG_CHECK(total_rows >= 0 && K > 0 && N > 0 && num_experts >= 1 && num_weight_matrices >= 1);
+  LMOE_ARG_CHECK(segment_expert || num_experts <= num_weight_matrices);
   LMOE_ARG_CHECK(input && packed && expert_offsets && output);
   LMOE_ARG_CHECK(aligned16(input) && aligned16(packed));
   LMOE_ARG_CHECK(epilogue >= kModePlain && epilogue <= kModeScatter);
@@ -367,6 +385,7 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
   p.offsets_i64 = offsets_are_int64;
   p.num_experts = num_experts;
   p.seg_expert = segment_expert;
+  p.num_w = num_weight_matrices;
   p.wq = packed;
   p.group_size = group_size;
   p.N = N;
@@ -387,6 +406,7 @@ extern "C" int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, in
     d.offsets_i64 = offsets_are_int64;
     d.num_experts = num_experts;
     d.seg_expert = segment_expert;
+    d.num_w = num_weight_matrices;
     d.wq = packed;
     d.group_size = group_size;
     d.N = N;
@@ -477,6 +497,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
     d1.K = d;
     d1.offsets = offx;
     d1.num_experts = E + S;
+    d1.num_w = E + S;
     d1.wq = w13_packed;
     d1.group_size = group_size;
     d1.N = 2 * F;
@@ -518,6 +539,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   g1.K = d;
   g1.offsets = offx;
   g1.num_experts = E + S;
+  g1.num_w = E + S;
   g1.wq = w13_packed;
   g1.group_size = group_size;
   g1.N = 2 * F;
@@ -535,6 +557,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   g2.K = F;
   g2.offsets = offx;
   g2.num_experts = E + S;
+  g2.num_w = E + S;
   g2.wq = w2_packed;
   g2.group_size = group_size;
   g2.N = d;

@@ -196,6 +196,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t M, uint32_t N) {
          | ((M >> 4) << 24);  // M / 16
 }
 
+// The same with A and B both fp16 (ab_f16 != 0) or both bf16: kind::f16 takes one type for
+// both operands.
+__host__ __device__ constexpr uint32_t idesc_f16kind_f32(uint32_t M, uint32_t N, int ab_f16) {
+  return ab_f16 ? (idesc_bf16_f32(M, N) & ~((7u << 7) | (7u << 10))) : idesc_bf16_f32(M, N);
+}
+
 // Shared-memory matrix descriptor for a K-major operand stored with the 128-byte swizzle:
 // rows of 128 bytes (64 bf16), groups of 8 rows 1024 bytes apart.  The tile base must be
 // 1024-byte aligned; advancing along K inside the 128-byte row is done by adding the byte

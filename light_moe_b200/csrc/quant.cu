@@ -131,13 +131,14 @@ extern "C" int lmoe_dequantize_w4(const uint8_t* qweight, const uint16_t* scales
   return cuda_status(cudaGetLastError());
 }
 
-extern "C" int lmoe_permute_rows(const void* hidden, const int32_t* sorted_idx, int64_t rows, int hidden_size,
-                                 int top_k, void* permuted, lmoe_stream_t stream_) {
+extern "C" int lmoe_permute_rows(const void* hidden, int elem_bytes, const int32_t* sorted_idx, int64_t rows,
+                                 int hidden_size, int top_k, void* permuted, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  LMOE_ARG_CHECK(rows >= 0 && hidden_size > 0 && (hidden_size % 8) == 0 && top_k >= 1);
+  LMOE_ARG_CHECK(elem_bytes == 2 || elem_bytes == 4);
+  LMOE_ARG_CHECK(rows >= 0 && hidden_size > 0 && ((int64_t)hidden_size * elem_bytes) % 16 == 0 && top_k >= 1);
   if (rows == 0) return LMOE_OK;
   LMOE_ARG_CHECK(hidden && sorted_idx && permuted && aligned16(hidden) && aligned16(permuted));
-  const int vec = hidden_size / 8;
+  const int vec = (int)(((int64_t)hidden_size * elem_bytes) / 16);   // 16-byte pieces per row
   const int threads = vec >= 256 ? 256 : ((vec + 31) / 32) * 32;
   const int64_t grid = rows < 65535 * 4 ? rows : 65535 * 4;
   permute_rows_kernel<<<(unsigned)grid, threads, 0, stream>>>(static_cast<const uint4*>(hidden), sorted_idx, rows,

@@ -66,6 +66,7 @@ struct RouterArgs {
   uint32_t w_box_bytes;   // one W tile [Epad x kBK]
   uint32_t tmem_cols;
   int do_perm;
+  int ab_f16;             // x and W are fp16 (else bf16) on the tensor-core path
 };
 
 struct __align__(8) RouterHdr {
@@ -95,6 +96,133 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Permutation phase, run once every tile's counts and bitmaps are in global memory: the
+// per-expert totals and, for each tile this CTA owns (blockIdx.x + i * gridDim.x), the
+// count of earlier tiles, from the [num_tiles, E] count table staged through shared memory
+// in chunks of tiles (16-byte loads, all of a thread's loads in flight at once); thread e
+// walks column e of a chunk in tile order.  Integer sums: the result is order-exact.  Then
+// the exclusive scan of the totals and the scatter of this CTA's tokens into sorted_idx
+// (rank of a token within its tile and expert = popcount of the lower bits of the bitmap).
+// `area` holds area_ints ints of shared memory (16-byte aligned); NT threads take part.
+template <int KMAX, int NT>
+__device__ __forceinline__ void perm_phase(const RouterArgs& a, int32_t* area, int area_ints, int32_t* total,
+                                           int32_t* offs) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int own_max = (a.num_tiles + (int)gridDim.x - 1) / (int)gridDim.x;
+  int32_t* pref = area;                              // [own tiles, E]
+  const int pref_ints = (own_max * a.E + 3) & ~3;
+  int32_t* chunk = pref + pref_ints;                 // [chunk tiles, E], 16-byte aligned
+  const int chunk_ints = area_ints - pref_ints;
+  const int chunk_tiles = min(((chunk_ints / a.E) & ~3), (a.num_tiles + 3) & ~3);   // >= 4 (host)
+  constexpr int kEPer = (kMaxExperts + NT - 1) / NT;
+  int32_t run[kEPer];
+#pragma unroll
+  for (int j = 0; j < kEPer; ++j) run[j] = 0;
+  for (int c0 = 0; c0 < a.num_tiles; c0 += chunk_tiles) {
+    const int nt = min(chunk_tiles, a.num_tiles - c0);
+    const int n = nt * a.E;
+    const int32_t* src = a.tile_counts + (int64_t)c0 * a.E;   // c0 * E * 4 is 16-byte aligned
+    constexpr int kBatch = 8;
+    for (int i0 = tid * 4; i0 < n; i0 += NT * 4 * kBatch) {
+      int4 v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * NT * 4;
+        if (i + 3 < n) v[u] = __ldcg(reinterpret_cast<const int4*>(src + i));
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * NT * 4;
+        if (i + 3 < n) {
+          *reinterpret_cast<int4*>(chunk + i) = v[u];
+        } else {
+          for (int r = i; r < n; ++r) chunk[r] = __ldcg(src + r);   // ragged tail (E % 4 != 0)
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kEPer; ++j) {
+      const int e = tid + j * NT;
+      if (e < a.E) {
+        int32_t r = run[j];
+        int own = (c0 + (int)gridDim.x - 1 - (int)blockIdx.x) / (int)gridDim.x;   // owned tiles before c0
+        int next = (int)blockIdx.x + own * (int)gridDim.x;                      // next owned tile
+        for (int tt = 0; tt < nt; ++tt) {
+          const int tile = c0 + tt;
+          if (tile == next) {
+            pref[own * a.E + e] = r;
+            ++own;
+            next += (int)gridDim.x;
+          }
+          r += chunk[tt * a.E + e];
+        }
+        run[j] = r;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < kEPer; ++j) {
+    const int e = tid + j * NT;
+    if (e < a.E) total[e] = run[j];
+  }
+  __syncthreads();
+  // exclusive scan of the per-expert totals: warp 0, 32 experts per round
+  if (warp == 0) {
+    int32_t run = 0;
+    for (int e0 = 0; e0 < a.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int32_t c = e < a.E ? total[e] : 0;
+      const int32_t v = warp_inclusive_scan(c, lane);
+      if (e < a.E) offs[e] = run + v - c;
+      run += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) offs[a.E] = run;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = tid; e < a.E; e += NT) {
+      a.counts[e] = total[e];
+      a.offsets[e] = offs[e];
+    }
+    if (tid == 0) a.offsets[a.E] = offs[a.E];
+  }
+  int own = 0;
+  for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++own) {
+    for (int row = tid; row < a.bm; row += NT) {
+      const int64_t t = (int64_t)tile * a.bm + row;
+      if (t >= a.T) continue;
+      const int w = row >> 5;
+      const uint32_t below = (1u << (row & 31)) - 1u;
+      // the row's k expert ids, then their k tile bitmaps: two rounds of loads in flight
+      int ev[KMAX];
+      uint4 bv[KMAX];
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (j < a.k) ev[j] = __ldcg(&a.ids[t * a.k + j]);
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (j < a.k) bv[j] = __ldcg(reinterpret_cast<const uint4*>(a.tile_bits) + (int64_t)tile * a.E + ev[j]);
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j) {
+        if (j < a.k) {
+          const uint32_t b[4] = {bv[j].x, bv[j].y, bv[j].z, bv[j].w};
+          int rank = __popc(b[w] & below);
+#pragma unroll
+          for (int i = 0; i < 3; ++i)
+            if (i < w) rank += __popc(b[i]);
+          const int32_t pos = offs[ev[j]] + pref[own * a.E + ev[j]] + rank;
+          a.sorted_idx[pos] = (int32_t)(t * a.k + j);
+          if (a.positions) a.positions[t * a.k + j] = pos;
+        }
+      }
+    }
+  }
 }
 
 template <int KMAX>
@@ -174,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, a.Epad);
+      const uint32_t idesc = idesc_f16kind_f32(kBM, a.Epad, a.ab_f16);
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++lt) {
@@ -381,123 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
     }
     __syncthreads();
-    if (!*abort_flag) {
-      // per-expert totals and, for each tile owned by this CTA, the count of earlier tiles.
-      // The [num_tiles, E] count table is staged through shared memory in chunks of tiles
-      // (16-byte loads, all of a thread's loads in flight at once); then thread e walks
-      // column e of the chunk in tile order.  Integer sums: the result is order-exact.
-      const int own_max = (a.num_tiles + (int)gridDim.x - 1) / (int)gridDim.x;
-      int32_t* pref = reinterpret_cast<int32_t*>(base);  // [own tiles, E] in the stage area
-      const int pref_ints = (own_max * a.E + 3) & ~3;
-      int32_t* chunk = pref + pref_ints;                 // [chunk tiles, E], 16-byte aligned
-      const int area_ints = (int)(((size_t)a.stages * a.stage_bytes) / 4) - pref_ints;
-      const int chunk_tiles = min(((area_ints / a.E) & ~3), (a.num_tiles + 3) & ~3);   // >= 4 (host)
-      constexpr int kEPer = (kMaxExperts + kThreads - 1) / kThreads;
-      int32_t run[kEPer];
-#pragma unroll
-      for (int j = 0; j < kEPer; ++j) run[j] = 0;
-      for (int c0 = 0; c0 < a.num_tiles; c0 += chunk_tiles) {
-        const int nt = min(chunk_tiles, a.num_tiles - c0);
-        const int n = nt * a.E;
-        const int32_t* src = a.tile_counts + (int64_t)c0 * a.E;   // c0 * E * 4 is 16-byte aligned
-        constexpr int kBatch = 8;
-        for (int i0 = tid * 4; i0 < n; i0 += kThreads * 4 * kBatch) {
-          int4 v[kBatch];
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            const int i = i0 + u * kThreads * 4;
-            if (i + 3 < n) v[u] = __ldcg(reinterpret_cast<const int4*>(src + i));
-          }
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            const int i = i0 + u * kThreads * 4;
-            if (i + 3 < n) {
-              *reinterpret_cast<int4*>(chunk + i) = v[u];
-            } else {
-              for (int r = i; r < n; ++r) chunk[r] = __ldcg(src + r);   // ragged tail (E % 4 != 0)
-            }
-          }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < kEPer; ++j) {
-          const int e = tid + j * kThreads;
-          if (e < a.E) {
-            int32_t r = run[j];
-            int own = (c0 + (int)gridDim.x - 1 - (int)blockIdx.x) / (int)gridDim.x;   // owned tiles before c0
-            int next = (int)blockIdx.x + own * (int)gridDim.x;                      // next owned tile
-            for (int tt = 0; tt < nt; ++tt) {
-              const int tile = c0 + tt;
-              if (tile == next) {
-                pref[own * a.E + e] = r;
-                ++own;
-                next += (int)gridDim.x;
-              }
-              r += chunk[tt * a.E + e];
-            }
-            run[j] = r;
-          }
-        }
-        __syncthreads();
-      }
-#pragma unroll
-      for (int j = 0; j < kEPer; ++j) {
-        const int e = tid + j * kThreads;
-        if (e < a.E) h->total[e] = run[j];
-      }
-      __syncthreads();
-      // exclusive scan of the per-expert totals: warp 0, 32 experts per round
-      if (warp == 0) {
-        int32_t run = 0;
-        for (int e0 = 0; e0 < a.E; e0 += 32) {
-          const int e = e0 + lane;
-          const int32_t c = e < a.E ? h->total[e] : 0;
-          const int32_t v = warp_inclusive_scan(c, lane);
-          if (e < a.E) h->offs[e] = run + v - c;
-          run += __shfl_sync(0xffffffffu, v, 31);
-        }
-        if (lane == 0) h->offs[a.E] = run;
-      }
-      __syncthreads();
-      if (blockIdx.x == 0) {
-        for (int e = tid; e < a.E; e += kThreads) {
-          a.counts[e] = h->total[e];
-          a.offsets[e] = h->offs[e];
-        }
-        if (tid == 0) a.offsets[a.E] = h->offs[a.E];
-      }
-      int own = 0;
-      for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++own) {
-        for (int row = tid; row < a.bm; row += kThreads) {
-          const int64_t t = (int64_t)tile * a.bm + row;
-          if (t >= a.T) continue;
-          const int w = row >> 5;
-          const uint32_t below = (1u << (row & 31)) - 1u;
-          // the row's k expert ids, then their k tile bitmaps: two rounds of loads in flight
-          int ev[KMAX];
-          uint4 bv[KMAX];
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j)
-            if (j < a.k) ev[j] = __ldcg(&a.ids[t * a.k + j]);
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j)
-            if (j < a.k) bv[j] = __ldcg(reinterpret_cast<const uint4*>(a.tile_bits) + (int64_t)tile * a.E + ev[j]);
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j) {
-            if (j < a.k) {
-              const uint32_t b[4] = {bv[j].x, bv[j].y, bv[j].z, bv[j].w};
-              int rank = __popc(b[w] & below);
-#pragma unroll
-              for (int i = 0; i < 3; ++i)
-                if (i < w) rank += __popc(b[i]);
-              const int32_t pos = h->offs[ev[j]] + pref[own * a.E + ev[j]] + rank;
-              a.sorted_idx[pos] = (int32_t)(t * a.k + j);
-              if (a.positions) a.positions[t * a.k + j] = pos;
-            }
-          }
-        }
-      }
-    }
+    if (!*abort_flag)
+      perm_phase<KMAX, kThreads>(a, reinterpret_cast<int32_t*>(base), (int)(((size_t)a.stages * a.stage_bytes) / 4),
+                                 h->total, h->offs);
   }
 
   __syncthreads();
@@ -508,40 +522,163 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// Small batches (at most kSmallTokens tokens, i.e. one 128-token tile): the tensor-core
-// kernel above would run on a single SM, streaming the whole batch through one CTA.
-// Instead one warp per (token, expert) computes the logit as a CUDA-core dot product
-// (16-byte loads, fp32 accumulation, fixed butterfly reduction: deterministic), and one CTA
-// routes the tokens with the same arithmetic as the epilogue above and builds the stable
-// (expert, token, slot) permutation.
+// Logits on CUDA cores.
+//  * Small batches (at most kSmallTokens tokens, i.e. one 128-token tile): the tensor-core
+//    kernel above would run on a single SM, streaming the whole batch through one CTA.
+//    Instead one warp per (token, expert) computes the logit as a dot product (16-byte
+//    loads, fp32 accumulation, fixed butterfly reduction: deterministic).
+//  * Inputs that are not both bf16 or both fp16 (fp32 hidden states or gate weight, or a mix
+//    of types): the reference converts both operands to fp32 and multiplies them in fp32
+//    (csrc/fused_moe_ops.cu:158-159), which a kind::f16 tensor-core MMA cannot reproduce
+//    (it takes one 16-bit type for both operands).  A tiled fp32 FFMA GEMM computes the
+//    logits from the caller's values; each logit is one sequential fp32 sum over the hidden
+//    dimension (deterministic).
+// The routing itself (softmax / top-k / renormalise, counts, offsets, permutation) then
+// runs from the fp32 logits with the same arithmetic as the tensor-core epilogue.
 // ---------------------------------------------------------------------------------------
 constexpr int kSmallTokens = 128;
 
-__global__ void __launch_bounds__(256) router_small_logits_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                   const __nv_bfloat16* __restrict__ w,
+// Eight consecutive elements (16-byte aligned) as fp32.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(256) router_small_logits_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                                                                    const float* __restrict__ bias, int T, int d,
                                                                    int E, float* __restrict__ logits) {
   const int t = blockIdx.x;
   const int e = blockIdx.y * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T || e >= E) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * d);
-  const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)e * d);
+  const TX* xr = x + (int64_t)t * d;
+  const TW* wr = w + (int64_t)e * d;
   float acc = 0.0f;
   for (int i = lane; i < d / 8; i += 32) {
-    const uint4 xv = xr[i], wv = wr[i];
-    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    float xf[8], wf[8];
+    load8(xr + 8 * i, xf);
+    load8(wr + 8 * i, wf);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xa[j]));
-      const float2 wf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wa[j]));
-      acc = __fmaf_rn(xf.x, wf.x, acc);
-      acc = __fmaf_rn(xf.y, wf.y, acc);
-    }
+    for (int j = 0; j < 8; ++j) acc = __fmaf_rn(xf[j], wf[j], acc);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
   if (lane == 0) logits[(int64_t)t * E + e] = bias ? __fadd_rn(acc, bias[e]) : acc;
+}
+
+// logits[t, e] = sum_i x[t, i] * w[e, i] (+ bias[e]): tiles of TM tokens x EW experts, 32
+// hidden values per step staged in shared memory as fp32; each thread owns 4 tokens x 4
+// experts and adds the products of one logit in hidden order (fp32 FFMA).
+template <typename TX, typename TW, int TM, int EW>
+__global__ void __launch_bounds__((TM / 4) * (EW / 4)) router_simt_logits_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ bias, int T, int d, int E,
+    float* __restrict__ logits) {
+  constexpr int kNT = (TM / 4) * (EW / 4);
+  constexpr int kKS = 32;
+  __shared__ __align__(16) float xs[kKS][TM];
+  __shared__ __align__(16) float ws[kKS][EW];
+  const int tid = threadIdx.x;
+  const int tx = tid % (EW / 4);   // expert quad
+  const int ty = tid / (EW / 4);   // token quad
+  const int64_t t0 = (int64_t)blockIdx.x * TM;
+  const int e0 = blockIdx.y * EW;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  for (int k0 = 0; k0 < d; k0 += kKS) {
+    for (int i = tid; i < TM * (kKS / 8); i += kNT) {
+      const int r = i / (kKS / 8), seg = i % (kKS / 8);
+      float f[8];
+      if (t0 + r < T) {
+        load8(x + (t0 + r) * d + k0 + seg * 8, f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[seg * 8 + j][r] = f[j];
+    }
+    for (int i = tid; i < EW * (kKS / 8); i += kNT) {
+      const int r = i / (kKS / 8), seg = i % (kKS / 8);
+      float f[8];
+      if (e0 + r < E) {
+        load8(w + (int64_t)(e0 + r) * d + k0 + seg * 8, f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ws[seg * 8 + j][r] = f[j];
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kKS; ++kk) {
+      const float4 xv = *reinterpret_cast<const float4*>(&xs[kk][ty * 4]);
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[kk][tx * 4]);
+      const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx * 4 + j;
+      if (e < E) logits[t * E + e] = bias ? __fadd_rn(acc[i][j], bias[e]) : acc[i][j];
+    }
+  }
+}
+
+// Softmax / top-k / renormalisation of one token's fp32 logits, the same operation sequence
+// as the tensor-core epilogue: max, sum of exp(l - max) in expert order, reciprocal,
+// probabilities into the insertion top-k, reciprocal of the sum of the k selected.
+template <int KMAX>
+__device__ __forceinline__ void route_row(const float* __restrict__ l, int E, int k, float (&tv)[KMAX],
+                                          int (&ti)[KMAX], float& invs) {
+  float m = -INFINITY;
+  for (int e = 0; e < E; ++e) m = fmaxf(m, l[e]);
+  float sum = 0.0f;
+  for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, softmax_exp(__fsub_rn(l[e], m)));
+  const float inv = __frcp_rn(sum);
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
+  for (int e = 0; e < E; ++e) topk_insert<KMAX>(tv, ti, __fmul_rn(softmax_exp(__fsub_rn(l[e], m)), inv), e);
+  float ssum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j)
+    if (j < k) ssum = __fadd_rn(ssum, tv[j]);
+  invs = __frcp_rn(ssum);
 }
 
 template <int KMAX>
@@ -553,24 +690,9 @@ __global__ void __launch_bounds__(kSmallTokens) router_small_route_kernel(const 
   const int t = threadIdx.x;
   for (int e = t; e < E; e += blockDim.x) scnt[e] = 0;
   if (t < T) {
-    // same sequence as the tensor-core path's epilogue: max, sum of exp(l - max),
-    // reciprocal, probabilities into the insertion top-k, reciprocal renormalisation
-    const float* l = logits + (int64_t)t * E;
-    float m = -INFINITY;
-    for (int e = 0; e < E; ++e) m = fmaxf(m, l[e]);
-    float sum = 0.0f;
-    for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, softmax_exp(__fsub_rn(l[e], m)));
-    const float inv = __frcp_rn(sum);
-    float tv[KMAX];
+    float tv[KMAX], invs;
     int ti[KMAX];
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
-    for (int e = 0; e < E; ++e) topk_insert<KMAX>(tv, ti, __fmul_rn(softmax_exp(__fsub_rn(l[e], m)), inv), e);
-    float ssum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j)
-      if (j < k) ssum = __fadd_rn(ssum, tv[j]);
-    const float invs = __frcp_rn(ssum);
+    route_row<KMAX>(logits + (int64_t)t * E, E, k, tv, ti, invs);
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
       if (j < k) {
@@ -616,6 +738,51 @@ __global__ void __launch_bounds__(kSmallTokens) router_small_route_kernel(const 
       __syncwarp();
     }
   }
+}
+
+// Any batch size from fp32 logits: one 128-token tile per CTA, one token per thread; with
+// the permutation requested it writes the tile's per-expert counts and token bitmaps in the
+// tensor-core kernel's format, for router_perm_kernel.
+template <int KMAX>
+__global__ void __launch_bounds__(kBM) router_route_logits_kernel(const float* __restrict__ logits, RouterArgs a) {
+  __shared__ uint32_t bits[kMaxExperts * 4];
+  const int row = threadIdx.x;
+  const int tile = blockIdx.x;
+  const int64_t t = (int64_t)tile * kBM + row;
+  for (int i = row; i < a.E * 4; i += kBM) bits[i] = 0u;
+  __syncthreads();
+  if (t < a.T) {
+    float tv[KMAX], invs;
+    int ti[KMAX];
+    route_row<KMAX>(logits + t * a.E, a.E, a.k, tv, ti, invs);
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < a.k) {
+        const float w = __fmul_rn(tv[j], invs);
+        a.ids[t * a.k + j] = ti[j];
+        if (a.weights) a.weights[t * a.k + j] = w;
+        if (a.weights_bf16) a.weights_bf16[t * a.k + j] = __float2bfloat16_rn(w);
+        if (a.do_perm) atomicOr(&bits[ti[j] * 4 + (row >> 5)], 1u << (row & 31));
+      }
+    }
+  }
+  if (!a.do_perm) return;
+  __syncthreads();
+  for (int e = row; e < a.E; e += kBM) {
+    const uint4 bv = make_uint4(bits[e * 4], bits[e * 4 + 1], bits[e * 4 + 2], bits[e * 4 + 3]);
+    a.tile_counts[(int64_t)tile * a.E + e] = __popc(bv.x) + __popc(bv.y) + __popc(bv.z) + __popc(bv.w);
+    reinterpret_cast<uint4*>(a.tile_bits)[(int64_t)tile * a.E + e] = bv;
+  }
+}
+
+// The permutation phase of the tensor-core kernel as a kernel of its own (launched after
+// router_route_logits_kernel on the same stream, so no grid barrier is needed).
+template <int KMAX>
+__global__ void __launch_bounds__(kThreads) router_perm_kernel(RouterArgs a, int area_ints) {
+  extern __shared__ int4 perm_area[];
+  __shared__ int32_t total[kMaxExperts];
+  __shared__ int32_t offs[kMaxExperts + 1];
+  perm_phase<KMAX, kThreads>(a, reinterpret_cast<int32_t*>(perm_area), area_ints, total, offs);
 }
 
 // Tile height: 128 tokens, or fewer when there are fewer than 128 tokens per SM, so that
@@ -674,23 +841,34 @@ static __device__ __align__(256) uint8_t g_router_scratch[kStaticScratchBytes];
 
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[kMaxScratchDevices] = {};
+struct ScratchSlot {
+  unsigned long long ctx_id;   // CUDA context the address belongs to (0 = none yet)
+  void* ptr;
+};
+ScratchSlot g_scratch[kMaxScratchDevices] = {};
 
-// Device address of g_router_scratch on the current device, looked up once per device (the
-// first call on a device does the lookup; later calls only read the cached pointer).
+// Device address of g_router_scratch in the current device's current context.  The lookup
+// runs on the first call in a context and again whenever the context changes (for example
+// after cudaDeviceReset made a new primary context); other calls only read the cached
+// pointer.
 int router_scratch(void** out) {
   int dev = 0;
   LMOE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxScratchDevices) return LMOE_ERR_UNSUPPORTED;
+  unsigned long long ctx = 0;
+  int st = current_context_id(&ctx);
+  if (st != LMOE_OK) return st;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (ctx == 0 || g_scratch[dev].ctx_id != ctx || !g_scratch[dev].ptr) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);   // binds the primary context
     if (e != cudaSuccess) return cuda_status(e);
     if (!p) return LMOE_ERR_DEVICE;
-    g_scratch_ptr[dev] = p;
+    st = current_context_id(&ctx);
+    if (st != LMOE_OK) return st;
+    g_scratch[dev] = {ctx, p};
   }
-  *out = g_scratch_ptr[dev];
+  *out = g_scratch[dev].ptr;
   return LMOE_OK;
 }
 
@@ -699,25 +877,116 @@ int router_scratch(void** out) {
 
 using namespace lmoe;
 
-extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts) {
-  if (num_tokens < 0 || num_experts <= 0) return 0;
-  const int64_t tiles = router_max_tiles(num_tokens);
-  size_t bytes = 256;                                   // error word + grid barrier counter
-  bytes += (size_t)tiles * num_experts * sizeof(int32_t);
-  bytes = (bytes + 255) & ~size_t(255);
-  bytes += (size_t)tiles * num_experts * 4 * sizeof(uint32_t);
-  // small batches keep the fp32 logits after the 256-byte header
-  const size_t small = num_tokens <= kSmallTokens ? 256 + (((size_t)num_tokens * num_experts * 4 + 255) & ~size_t(255)) : 0;
-  return bytes > small ? bytes : small;
+namespace {
+
+bool dtype_ok(int dt) { return dt == LMOE_DTYPE_BF16 || dt == LMOE_DTYPE_F16 || dt == LMOE_DTYPE_F32; }
+
+// Both operands bf16, or both fp16: the tensor-core kernel computes the logits.
+bool tensor_core_logits(int x_dtype, int w_dtype) {
+  return x_dtype == w_dtype && (x_dtype == LMOE_DTYPE_BF16 || x_dtype == LMOE_DTYPE_F16);
 }
 
-extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
-                                    int64_t num_tokens, int hidden_size, int num_experts, int top_k,
-                                    int32_t* ids, float* weights, void* weights_bf16, int32_t* counts,
-                                    int32_t* offsets, int32_t* sorted_idx, int32_t* positions, float* logits,
-                                    void* workspace,
-                                    size_t workspace_bytes, lmoe_stream_t stream_) {
+// Bytes of the per-tile count table and bitmaps (after the 256-byte header).
+size_t router_tile_bytes(int64_t tiles, int E) {
+  size_t bytes = 256 + (size_t)tiles * E * sizeof(int32_t);   // error word, grid barrier, counts
+  bytes = (bytes + 255) & ~size_t(255);
+  return bytes + (size_t)tiles * E * 4 * sizeof(uint32_t);
+}
+
+template <typename TX, typename TW>
+int launch_logits(const void* hidden, const void* gate_weight, const float* bias, int64_t T, int d, int E,
+                  float* logits, cudaStream_t stream) {
+  const TX* x = static_cast<const TX*>(hidden);
+  const TW* w = static_cast<const TW*>(gate_weight);
+  if (T <= kSmallTokens) {
+    router_small_logits_kernel<TX, TW><<<dim3((unsigned)T, (E + 7) / 8), 256, 0, stream>>>(x, w, bias, (int)T, d, E,
+                                                                                            logits);
+  } else if (E <= 16) {
+    router_simt_logits_kernel<TX, TW, 128, 16>
+        <<<dim3((unsigned)((T + 127) / 128), 1), 128, 0, stream>>>(x, w, bias, (int)T, d, E, logits);
+  } else {
+    router_simt_logits_kernel<TX, TW, 64, 64>
+        <<<dim3((unsigned)((T + 63) / 64), (E + 63) / 64), 256, 0, stream>>>(x, w, bias, (int)T, d, E, logits);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename TX>
+int launch_logits_w(const void* hidden, const void* gate_weight, int w_dtype, const float* bias, int64_t T, int d,
+                    int E, float* logits, cudaStream_t stream) {
+  if (w_dtype == LMOE_DTYPE_BF16) return launch_logits<TX, __nv_bfloat16>(hidden, gate_weight, bias, T, d, E, logits, stream);
+  if (w_dtype == LMOE_DTYPE_F16) return launch_logits<TX, __half>(hidden, gate_weight, bias, T, d, E, logits, stream);
+  return launch_logits<TX, float>(hidden, gate_weight, bias, T, d, E, logits, stream);
+}
+
+int launch_logits_any(const void* hidden, int x_dtype, const void* gate_weight, int w_dtype, const float* bias,
+                      int64_t T, int d, int E, float* logits, cudaStream_t stream) {
+  if (x_dtype == LMOE_DTYPE_BF16)
+    return launch_logits_w<__nv_bfloat16>(hidden, gate_weight, w_dtype, bias, T, d, E, logits, stream);
+  if (x_dtype == LMOE_DTYPE_F16) return launch_logits_w<__half>(hidden, gate_weight, w_dtype, bias, T, d, E, logits, stream);
+  return launch_logits_w<float>(hidden, gate_weight, w_dtype, bias, T, d, E, logits, stream);
+}
+
+template <int KMAX>
+int launch_route_from_logits(const float* lg, RouterArgs a, int num_sms, cudaStream_t stream) {
+  if (a.T <= kSmallTokens) {
+    router_small_route_kernel<KMAX><<<1, kSmallTokens, 0, stream>>>(lg, a.T, a.E, a.k, a);
+    return cuda_status(cudaGetLastError());
+  }
+  router_route_logits_kernel<KMAX><<<a.num_tiles, kBM, 0, stream>>>(lg, a);
+  LMOE_CUDA_TRY(cudaGetLastError());
+  if (!a.do_perm) return LMOE_OK;
+  // the permutation kernel's shared area: the owned tiles' prefixes and a chunk of count rows
+  const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
+  const int own_max = (a.num_tiles + grid - 1) / grid;
+  const int pref_ints = (own_max * a.E + 3) & ~3;
+  int chunk_tiles = (((64 * 1024) / 4) / a.E) & ~3;
+  chunk_tiles = chunk_tiles < 4 ? 4 : chunk_tiles;
+  const int area_ints = pref_ints + chunk_tiles * a.E;
+  const size_t smem = (size_t)area_ints * sizeof(int32_t);
+  auto fn = router_perm_kernel<KMAX>;
+  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+  if (st != LMOE_OK) return st;
+  fn<<<grid, kThreads, smem, stream>>>(a, area_ints);
+  return cuda_status(cudaGetLastError());
+}
+
+int route_from_logits(const float* lg, const RouterArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.k <= 2) return launch_route_from_logits<2>(lg, a, num_sms, stream);
+  if (a.k <= 4) return launch_route_from_logits<4>(lg, a, num_sms, stream);
+  if (a.k <= 8) return launch_route_from_logits<8>(lg, a, num_sms, stream);
+  return launch_route_from_logits<16>(lg, a, num_sms, stream);
+}
+
+}  // namespace
+
+extern "C" size_t lmoe_router_workspace_bytes_typed(int64_t num_tokens, int num_experts, int x_dtype, int w_dtype) {
+  if (num_tokens < 0 || num_experts <= 0 || !dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return 0;
+  const size_t logits = (((size_t)num_tokens * num_experts * sizeof(float)) + 255) & ~size_t(255);
+  if (num_tokens <= kSmallTokens) {
+    // the fp32 logits after the 256-byte header
+    const size_t small = 256 + logits;
+    const size_t tiles = router_tile_bytes(router_max_tiles(num_tokens), num_experts);
+    return tiles > small ? tiles : small;
+  }
+  if (tensor_core_logits(x_dtype, w_dtype)) return router_tile_bytes(router_max_tiles(num_tokens), num_experts);
+  // CUDA-core logits: 128-token tiles, then the fp32 logits
+  const size_t tiles = (router_tile_bytes((num_tokens + kBM - 1) / kBM, num_experts) + 255) & ~size_t(255);
+  return tiles + logits;
+}
+
+extern "C" size_t lmoe_router_workspace_bytes(int64_t num_tokens, int num_experts) {
+  return lmoe_router_workspace_bytes_typed(num_tokens, num_experts, LMOE_DTYPE_BF16, LMOE_DTYPE_BF16);
+}
+
+extern "C" int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const void* gate_weight, int w_dtype,
+                                          const float* gate_bias, int64_t num_tokens, int hidden_size,
+                                          int num_experts, int top_k, int32_t* ids, float* weights,
+                                          void* weights_bf16, int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
+                                          int32_t* positions, float* logits, void* workspace, size_t workspace_bytes,
+                                          lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  LMOE_ARG_CHECK(dtype_ok(x_dtype) && dtype_ok(w_dtype));
   LMOE_ARG_CHECK(num_tokens >= 0 && num_tokens <= (int64_t)INT32_MAX / 16);
   LMOE_ARG_CHECK(num_experts >= 1 && num_experts <= kMaxExperts);
   LMOE_ARG_CHECK(top_k >= 1 && top_k <= 16 && top_k <= num_experts);
@@ -735,7 +1004,7 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   LMOE_ARG_CHECK(ids != nullptr);
   if (do_perm) LMOE_ARG_CHECK(counts && offsets && sorted_idx);
   LMOE_ARG_CHECK(hidden && gate_weight && aligned16(hidden) && aligned16(gate_weight));
-  const size_t need = lmoe_router_workspace_bytes(num_tokens, num_experts);
+  const size_t need = lmoe_router_workspace_bytes_typed(num_tokens, num_experts, x_dtype, w_dtype);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
 
   DeviceInfo dev;
@@ -744,10 +1013,10 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   if (dev.cc_major != 10) return LMOE_ERR_DEVICE;
 
   const int E = num_experts;
-  if (num_tokens <= kSmallTokens) {
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (num_tokens <= kSmallTokens || !tensor_core_logits(x_dtype, w_dtype)) {
+    // CUDA-core logits into the caller's buffer or the workspace, then routing from them
     LMOE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, stream));
-    float* lg = logits ? logits : reinterpret_cast<float*>(ws + 256);
     RouterArgs a = {};
     a.ids = ids;
     a.weights = weights;
@@ -757,16 +1026,29 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
     a.sorted_idx = sorted_idx;
     a.positions = do_perm ? positions : nullptr;
     a.do_perm = do_perm ? 1 : 0;
-    const int T = (int)num_tokens;
-    router_small_logits_kernel<<<dim3(T, (E + 7) / 8), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(gate_weight), gate_bias, T,
-        hidden_size, E, lg);
-    LMOE_CUDA_TRY(cudaGetLastError());
-    if (top_k <= 2) router_small_route_kernel<2><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
-    else if (top_k <= 4) router_small_route_kernel<4><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
-    else if (top_k <= 8) router_small_route_kernel<8><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
-    else router_small_route_kernel<16><<<1, kSmallTokens, 0, stream>>>(lg, T, E, top_k, a);
-    return cuda_status(cudaGetLastError());
+    a.err = reinterpret_cast<uint32_t*>(ws);
+    a.T = (int)num_tokens;
+    a.d = hidden_size;
+    a.E = E;
+    a.k = top_k;
+    a.bm = kBM;
+    a.num_tiles = (int)((num_tokens + kBM - 1) / kBM);
+    float* lg = logits;
+    if (!lg) {
+      const size_t off = num_tokens <= kSmallTokens
+                             ? 256
+                             : (router_tile_bytes(a.num_tiles, E) + 255) & ~size_t(255);
+      lg = reinterpret_cast<float*>(ws + off);
+    }
+    if (num_tokens > kSmallTokens) {
+      a.tile_counts = reinterpret_cast<int32_t*>(ws + 256);
+      size_t tb_off = 256 + (size_t)a.num_tiles * E * sizeof(int32_t);
+      tb_off = (tb_off + 255) & ~size_t(255);
+      a.tile_bits = reinterpret_cast<uint32_t*>(ws + tb_off);
+    }
+    st = launch_logits_any(hidden, x_dtype, gate_weight, w_dtype, gate_bias, num_tokens, hidden_size, E, lg, stream);
+    if (st != LMOE_OK) return st;
+    return route_from_logits(lg, a, dev.num_sms, stream);
   }
   const int Epad = ((E + 15) / 16) * 16;
   const int bm = router_tile_rows(num_tokens, dev.num_sms);
@@ -792,9 +1074,8 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
     if ((pref_ints + 4 * (size_t)E) * sizeof(int32_t) > (size_t)stages * stage_bytes) return LMOE_ERR_UNSUPPORTED;
   }
 
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
   LMOE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, stream));
-  RouterArgs a;
+  RouterArgs a = {};
   a.bias = gate_bias;
   a.ids = ids;
   a.weights = weights;
@@ -823,18 +1104,31 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
   a.tmem_cols = tmem_cols;
   a.do_perm = do_perm ? 1 : 0;
 
+  a.ab_f16 = x_dtype == LMOE_DTYPE_F16 ? 1 : 0;
+
+  const CUtensorMapDataType tdt = a.ab_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tm_x, tm_w;
-  st = encode_tmap_2d(&tm_x, hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)num_tokens,
-                      (uint64_t)hidden_size, (uint64_t)hidden_size * 2, (uint32_t)bm, kBK, true);
+  st = encode_tmap_2d(&tm_x, hidden, tdt, 2, (uint64_t)num_tokens, (uint64_t)hidden_size, (uint64_t)hidden_size * 2,
+                      (uint32_t)bm, kBK, true);
   if (st != LMOE_OK) return st;
-  st = encode_tmap_2d(&tm_w, gate_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E, (uint64_t)hidden_size,
-                      (uint64_t)hidden_size * 2, (uint32_t)Epad, kBK, true);
+  st = encode_tmap_2d(&tm_w, gate_weight, tdt, 2, (uint64_t)E, (uint64_t)hidden_size, (uint64_t)hidden_size * 2,
+                      (uint32_t)Epad, kBK, true);
   if (st != LMOE_OK) return st;
 
   if (top_k <= 2) return launch_router<2>(tm_x, tm_w, a, grid, smem, stream);
   if (top_k <= 4) return launch_router<4>(tm_x, tm_w, a, grid, smem, stream);
   if (top_k <= 8) return launch_router<8>(tm_x, tm_w, a, grid, smem, stream);
   return launch_router<16>(tm_x, tm_w, a, grid, smem, stream);
+}
+
+extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const float* gate_bias,
+                                    int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                                    int32_t* ids, float* weights, void* weights_bf16, int32_t* counts,
+                                    int32_t* offsets, int32_t* sorted_idx, int32_t* positions, float* logits,
+                                    void* workspace, size_t workspace_bytes, lmoe_stream_t stream) {
+  return lmoe_fused_gate_topk_typed(hidden, LMOE_DTYPE_BF16, gate_weight, LMOE_DTYPE_BF16, gate_bias, num_tokens,
+                                    hidden_size, num_experts, top_k, ids, weights, weights_bf16, counts, offsets,
+                                    sorted_idx, positions, logits, workspace, workspace_bytes, stream);
 }
 
 extern "C" int lmoe_fused_gate_topk_static(const void* hidden, const void* gate_weight, const float* gate_bias,

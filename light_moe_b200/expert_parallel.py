@@ -84,13 +84,20 @@ class ExpertParallelGroup:
         return self.attach()
 
     def attach(self, group: Optional[dist.ProcessGroup] = None):
-        """Use an existing process group (default: the world)."""
-        self.world_size = dist.get_world_size()
-        self.rank = dist.get_rank()
-        if self.world_size < self.ep_size:
-            raise ValueError(f"world size {self.world_size} < EP size {self.ep_size}")
-        if group is None and self.ep_size != self.world_size:
-            group = dist.new_group(list(range(self.ep_size)))
+        """Use an existing process group (default: the world, or its first ``ep_size`` ranks
+        when the world is larger -- every rank of the world must then call this, as
+        ``dist.new_group`` requires).  ``rank`` and ``world_size`` are this process's rank and
+        the size *within* the group; a process outside the group gets rank -1."""
+        if group is None:
+            ws = dist.get_world_size()
+            if ws < self.ep_size:
+                raise ValueError(f"world size {ws} < EP size {self.ep_size}")
+            if self.ep_size != ws:
+                group = dist.new_group(list(range(self.ep_size)))
+        self.world_size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world_size != self.ep_size:
+            raise ValueError(f"process group of {self.world_size} ranks for EP size {self.ep_size}")
         self.group = group
         self.initialized = True
         return self
@@ -126,7 +133,8 @@ class CudaExpertBackend:
     def gather(self, x, sorted_idx):
         from . import capi
         rows = torch.empty(sorted_idx.numel(), x.shape[1], dtype=x.dtype, device=x.device)
-        capi.call("lmoe_permute_rows", x.data_ptr(), sorted_idx.data_ptr(), sorted_idx.numel(), x.shape[1],
+        capi.call("lmoe_permute_rows", x.data_ptr(), x.element_size(), sorted_idx.data_ptr(), sorted_idx.numel(),
+                  x.shape[1],
                   self.top_k, rows.data_ptr(), capi.stream_handle())
         return rows
 
@@ -168,6 +176,8 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         """Build this rank's layer from the full (all-expert) prepacked weights."""
         ws = dist.get_world_size(group)
         g = ExpertParallelGroup(ws).attach(group)
+        if g.rank < 0:
+            raise ValueError("this process is not a member of the expert-parallel group")
         cfg = ExpertParallelConfig(num_experts=experts.num_experts, top_k=top_k, hidden_size=experts.hidden_size,
                                    intermediate_size=experts.ffn_size, ep_size=ws, group_size=experts.group_size,
                                    num_shared=experts.num_shared)
@@ -252,6 +262,8 @@ def slice_experts(ex: W4A16Experts, e0: int, e1: int) -> W4A16Experts:
 
     The prepacked layouts are expert-major, so an expert range is one contiguous slice.
     """
+    if not 0 <= e0 <= e1 <= ex.num_experts:
+        raise ValueError(f"expert range [{e0}, {e1}) outside the {ex.num_experts} routed experts")
     Et = ex.num_experts + ex.num_shared
 
     def part(t, idx):

@@ -33,7 +33,9 @@ from inputs import BLOCK_CASES, block_inputs, cfg1_inputs  # noqa: E402
 
 
 def _import_reference():
-    ref = os.environ.get("LIGHT_MOE_REF", "/root/reference/python")
+    ref = os.environ.get("LIGHT_MOE_REF")
+    if not ref:
+        raise SystemExit("set LIGHT_MOE_REF to the reference checkout's python/ directory")
     if ref not in sys.path:
         sys.path.insert(0, ref)
     import torch  # noqa: F401

@@ -18,10 +18,12 @@ def read_error(ws: torch.Tensor) -> int:
 
 
 def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
-    """lmoe_fused_gate_topk through the C ABI; returns numpy arrays."""
+    """lmoe_fused_gate_topk_typed through the C ABI (x and w of any of bf16 / fp16 / fp32);
+    returns numpy arrays."""
     T, d = x.shape
     E = w.shape[0]
     dev = x.device
+    xdt, wdt = capi.dtype_code(x.dtype), capi.dtype_code(w.dtype)
     ids = torch.empty(T, k, dtype=torch.int32, device=dev)
     wts = torch.empty(T, k, dtype=torch.float32, device=dev)
     wbf = torch.empty(T, k, dtype=torch.bfloat16, device=dev)
@@ -30,9 +32,10 @@ def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
     sidx = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if perm else None
     lg = torch.empty(T, E, dtype=torch.float32, device=dev) if logits else None
     pos = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if positions else None
-    nbytes = capi.lib().lmoe_router_workspace_bytes(T, E)
+    nbytes = capi.lib().lmoe_router_workspace_bytes_typed(T, E, xdt, wdt)
     ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
-    capi.call("lmoe_fused_gate_topk", x.data_ptr(), w.data_ptr(), capi.ptr(bias), T, d, E, k, ids.data_ptr(),
+    capi.call("lmoe_fused_gate_topk_typed", x.data_ptr(), xdt, w.data_ptr(), wdt, capi.ptr(bias), T, d, E, k,
+              ids.data_ptr(),
               wts.data_ptr(), wbf.data_ptr(), capi.ptr(counts), capi.ptr(offsets), capi.ptr(sidx), capi.ptr(pos),
               capi.ptr(lg),
               ws.data_ptr(), ws.numel(), stream())
@@ -83,14 +86,19 @@ def w4_gemm(x, packed, N, group_size, offsets, epilogue=0, dest=None, row_scale=
             hint=0, seg_expert=None, pad=0):
     """``pad`` extra output columns make the row stride ldo = ncols + pad (the returned view
     drops them; they must stay zero)."""
+    import ctypes
     R, K = x.shape
     E = offsets.numel() - 1
     ncols = N // 2 if epilogue == 1 else N
     rows_out = out_rows if out_rows is not None else R
     full = torch.zeros(rows_out, ncols + pad, dtype=torch.bfloat16, device=x.device)
     ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
+    per = ctypes.c_size_t()
+    capi.call("lmoe_w4_prepacked_bytes", 1, N, K, group_size, 0, ctypes.byref(per))
+    num_w = packed.numel() // per.value
     capi.call("lmoe_w4a16_grouped_gemm", x.data_ptr(), R, K, packed.data_ptr(), N, group_size,
-              offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, capi.ptr(seg_expert), epilogue,
+              offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, capi.ptr(seg_expert), num_w,
+              epilogue,
               capi.ptr(dest),
               capi.ptr(row_scale), hint, full.data_ptr(), ncols + pad, ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
@@ -108,6 +116,20 @@ def bf16_gemm(x, w, offsets, zero_fill=1):
     capi.call("lmoe_grouped_gemm_bf16", x.data_ptr(), R, K, w.data_ptr(), N, offsets.data_ptr(),
               1 if offsets.dtype == torch.int64 else 0, E, zero_fill, out.data_ptr(), ws.data_ptr(), ws.numel(),
               stream())
+    torch.cuda.synchronize()
+    assert read_error(ws) == 0
+    return out
+
+
+def dense_gemm(x, w, offsets, zero_fill=1):
+    """lmoe_grouped_gemm in the dtype of x (bf16 / fp16 / fp32)."""
+    R, K = x.shape
+    E, N, _ = w.shape
+    out = torch.empty(R, N, dtype=x.dtype, device=x.device)
+    ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
+    capi.call("lmoe_grouped_gemm", x.data_ptr(), capi.dtype_code(x.dtype), R, K, w.data_ptr(), N,
+              offsets.data_ptr(), 1 if offsets.dtype == torch.int64 else 0, E, zero_fill, out.data_ptr(),
+              ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     assert read_error(ws) == 0
     return out

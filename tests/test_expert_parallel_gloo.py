@@ -52,11 +52,20 @@ def _worker(rank, world, port, case, q):
                                                     ExpertParallelW4A16Layer)
         E, S, k, d, F, g, Ts = case["E"], case["S"], case["k"], case["d"], case["F"], case["g"], case["T"]
         gw, deq = _weights(E, S, d, F, g)
-        epr = E // world
-        idx = list(range(rank * epr, (rank + 1) * epr)) + list(range(E, E + S))
+        if case.get("subgroups"):
+            # two independent EP groups {0, 1} and {2, 3}: the layer must use its rank and size
+            # within its own group, not in the world
+            groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
+            ep = 2
+            grp = ExpertParallelGroup(ep).attach(groups[rank // 2])
+        else:
+            ep = world
+            grp = ExpertParallelGroup(world).attach()
+        epr = E // ep
+        gr = grp.rank
+        idx = list(range(gr * epr, (gr + 1) * epr)) + list(range(E, E + S))
         be = OracleExpertBackend(deq["w1"][idx], deq["w3"][idx], deq["w2"][idx], k, S)
-        grp = ExpertParallelGroup(world).attach()
-        cfg = ExpertParallelConfig(num_experts=E, top_k=k, hidden_size=d, intermediate_size=F, ep_size=world,
+        cfg = ExpertParallelConfig(num_experts=E, top_k=k, hidden_size=d, intermediate_size=F, ep_size=ep,
                                    group_size=g, num_shared=S)
         layer = ExpertParallelW4A16Layer(cfg, grp, torch.from_numpy(gw), be, micro_batches=case.get("mb", 1))
         x = np.random.default_rng(100 + rank).standard_normal((Ts[rank], d), dtype=np.float32)
@@ -102,6 +111,8 @@ def _run(world, case, timeout=120):
     (4, dict(E=8, S=0, k=3, d=64, F=64, g=64, T=[30, 2, 12, 25], mb=3)),
     # fine-grained routing shape: 64 experts (16 per rank), top-6, two shared experts
     (4, dict(E=64, S=2, k=6, d=64, F=64, g=64, T=[50, 9, 33, 20])),
+    # two EP groups of two ranks inside a world of four (ranks 2, 3 are ranks 0, 1 of theirs)
+    (4, dict(E=8, S=1, k=2, d=64, F=64, g=64, T=[20, 7, 13, 31], subgroups=True)),
 ])
 def test_expert_parallel_matches_single_process(world, case):
     results, codes = _run(world, case)
@@ -117,3 +128,16 @@ def test_rank_failure_is_reported_not_hung():
     results, codes = _run(2, case, timeout=90)
     assert codes[1] == 3
     assert 0 in results and results[0][0] == "error", results
+
+
+def test_slice_experts_rejects_ranges_outside_the_experts():
+    from light_moe_b200.expert_parallel import slice_experts
+    from light_moe_b200.layer import W4A16Experts
+    E, S = 4, 1
+    ex = W4A16Experts(torch.zeros((E + S) * 8, dtype=torch.uint8), torch.zeros((E + S) * 4, dtype=torch.uint8),
+                      E, S, 128, 128, 128)
+    part = slice_experts(ex, 2, 4)
+    assert part.num_experts == 2 and part.num_shared == 1 and part.w13_packed.numel() == 3 * 8
+    for e0, e1 in ((3, 5), (-1, 1), (3, 2)):
+        with pytest.raises(ValueError):
+            slice_experts(ex, e0, e1)

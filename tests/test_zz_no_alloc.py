@@ -26,24 +26,31 @@ def _outputs(T, E, k, dev):
 
 
 def _args(o):
-    return (o["ids"].data_ptr(), o["weights"].data_ptr(), o["weights_bf16"].data_ptr(), o["counts"].data_ptr(),
-            o["offsets"].data_ptr(), o["sorted_idx"].data_ptr(), o["positions"].data_ptr(), o["logits"].data_ptr())
+    names = ("ids", "weights", "weights_bf16", "counts", "offsets", "sorted_idx", "positions", "logits")
+    return tuple(capi.ptr(o.get(n)) for n in names)
 
 
-def _route_static(x, w, bias, k):
+def _select(o, perm, logits):
+    # leave out the permutation outputs (non-cooperative launch) and / or the logits (the
+    # small-batch path then keeps its fp32 logits in the scratch itself)
+    drop = (() if perm else ("counts", "offsets", "sorted_idx", "positions")) + (() if logits else ("logits",))
+    return {n: t for n, t in o.items() if n not in drop}
+
+
+def _route_static(x, w, bias, k, perm=True, logits=True):
     T, d = x.shape
     E = w.shape[0]
-    o = _outputs(T, E, k, x.device)
+    o = _select(_outputs(T, E, k, x.device), perm, logits)
     capi.call("lmoe_fused_gate_topk_static", x.data_ptr(), w.data_ptr(), capi.ptr(bias), T, d, E, k, *_args(o),
               capi.stream_handle())
     torch.cuda.synchronize()
     return {n: t.float().cpu().numpy() if t.dtype == torch.bfloat16 else t.cpu().numpy() for n, t in o.items()}
 
 
-def _route_workspace(x, w, bias, k):
+def _route_workspace(x, w, bias, k, perm=True, logits=True):
     T, d = x.shape
     E = w.shape[0]
-    o = _outputs(T, E, k, x.device)
+    o = _select(_outputs(T, E, k, x.device), perm, logits)
     nbytes = capi.lib().lmoe_router_workspace_bytes(T, E)
     ws = torch.zeros(nbytes, dtype=torch.uint8, device=x.device)
     capi.call("lmoe_fused_gate_topk", x.data_ptr(), w.data_ptr(), capi.ptr(bias), T, d, E, k, *_args(o),
@@ -60,20 +67,28 @@ def test_static_router_matches_workspace_router_on_consecutive_calls():
     dev = torch.device("cuda")
     # the second call is smaller and has fewer experts, so it runs on whatever the first
     # call left in the shared scratch
-    cases = [(STATIC_MAX_TOKENS, 1024, 64, 6, True), (333, 4096, 8, 2, False)]
-    for T, d, E, k, with_bias in cases:
+    # (T, d, E, k, bias, permutation outputs, logits output); T <= 128 runs the small-batch
+    # kernels, whose fp32 logits live in the scratch when the caller passes no logits buffer
+    cases = [(STATIC_MAX_TOKENS, 1024, 64, 6, True, True, True), (333, 4096, 8, 2, False, True, True),
+             (64, 4096, 8, 2, False, True, False), (64, 512, 16, 4, True, False, False),
+             (5000, 1024, 8, 2, True, False, True)]
+    for T, d, E, k, with_bias, perm, logits in cases:
         x = (torch.randn(T, d, device=dev) * 0.5).to(torch.bfloat16)
         w = (torch.randn(E, d, device=dev) * 0.02).to(torch.bfloat16)
         bias = torch.randn(E, device=dev) * 0.1 if with_bias else None
-        a = _route_static(x, w, bias, k)
-        b = _route_workspace(x, w, bias, k)
+        a = _route_static(x, w, bias, k, perm, logits)
+        b = _route_workspace(x, w, bias, k, perm, logits)
+        assert set(a) == set(b)
         # same kernel on the same inputs: the integer outputs are identical and the floating
         # ones agree to the bit (tolerance 0)
         for name in ("ids", "counts", "offsets", "sorted_idx", "positions"):
-            np.testing.assert_array_equal(a[name], b[name], err_msg=f"{name} T={T} E={E}")
+            if name in a:
+                np.testing.assert_array_equal(a[name], b[name], err_msg=f"{name} T={T} E={E}")
         for name in ("weights", "weights_bf16", "logits"):
-            np.testing.assert_allclose(a[name], b[name], rtol=0, atol=0, err_msg=f"{name} T={T} E={E}")
-        assert int(a["offsets"][-1]) == T * k
+            if name in a:
+                np.testing.assert_allclose(a[name], b[name], rtol=0, atol=0, err_msg=f"{name} T={T} E={E}")
+        if perm:
+            assert int(a["offsets"][-1]) == T * k
 
 
 def test_static_router_rejects_more_tokens_than_its_scratch_holds():
