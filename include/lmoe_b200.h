@@ -241,7 +241,7 @@ size_t lmoe_moe_layer_workspace_bytes(int64_t num_tokens, int hidden_size, int f
  *          (routed experts first), each 2*ffn_size x hidden_size
  * w2       prepacked down weights, each hidden_size x ffn_size
  * num_shared always-on experts (weight 1, every token), 0 for Mixtral
- * y        bf16 [num_tokens, hidden_size]
+ * y        bf16 [num_tokens, hidden_size], 8-byte aligned
  * ids_out / weights_out: optional copies of the routing (int32 / fp32 [num_tokens, top_k])
  */
 int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidden_size,

@@ -7,44 +7,40 @@
 // defined by this library, the reference only has the unused flag
 // python/light_moe/engine/executor.py:44-48).
 //
-// Why a second kernel.  With a handful of tokens per expert the GEMM is a weight stream:
-// 8.5 KB of int4 per 128 x 128 super-block, ~23 bytes per SM per cycle at HBM speed, i.e.
-// ~380 cycles per super-block.  Measured on B200:
-//   * a tcgen05.mma (M=128, K=16, N <= 128) costs ~44 cycles of issue per issuing thread,
-//     whatever N is; two threads issuing to separate accumulators overlap (~24 cycles per
-//     MMA per SM).  The eight MMAs of a super-block therefore fit the budget only with two
-//     issuers, so warp 2 issues k-block 0 and warp 3 k-block 1 of every stage.
-//   * dequantising with the scale folded in (bf16_rn(q * s), three fp16 ops per pair) does
-//     not fit next to the rest; here the dequantisers only turn nibbles into integer-valued
-//     bf16 q (one shift, one LOP3, one exact bf16 subtraction per pair), the MMAs write the
-//     per-k-block partial sums P = sum_k q * x into a tensor-memory ring, and the epilogue
-//     warps apply the fp16 scale in fp32: acc += s * P.  The result equals
-//     sum_k (q * s) * x up to fp32 rounding (it never rounds the weights to bf16).
-//
-//   * a tcgen05.commit costs about as much issue time as an MMA, and an mbarrier wait in
-//     the issuing thread ~270 cycles even when the phase has long completed, so an issuer
-//     polls a shared-memory counter (published by warp 16 after its barrier wait), issues
-//     its four MMAs and commits once per stage.  The q stage, the token stage and the
-//     partial-sum slot share one ring index; "stage ready" (a_full) collects the
-//     dequantisers' arrivals, the token TMA bytes and the epilogue's release of the slot's
-//     previous round, and "stage done" (mma_done) collects both issuers' commits and the
-//     dequantisers' "scales written" arrivals, so the epilogue also waits once per stage.
+// With a handful of tokens per expert the GEMM is a weight stream: 8.5 KB of int4 per
+// 128 x 128 super-block, ~22 bytes per SM per cycle at HBM speed, i.e. ~380 cycles per
+// super-block.  Costs measured on B200 that shape the pipeline:
+//   * a tcgen05.mma (M=128, K=16, N <= 128) blocks its issuing thread ~44 cycles whatever N
+//     is; two threads issuing to separate accumulators overlap (~24 cycles per MMA per SM);
+//   * a tcgen05.commit costs about as much issue time as an MMA; an mbarrier wait in an
+//     MMA-issuing thread ~270 cycles even on a completed phase, a shared-memory load ~40.
+// So:
+//   * the dequantisers only turn nibbles into integer-valued bf16 q (one shift, one LOP3 and
+//     one exact bf16 subtraction per pair) in tensor memory; the MMAs write the partial sum
+//     P = sum_k q * x of each 128-K stage (one scale group) into a tensor-memory slot and the
+//     epilogue warps apply the fp16 scale in fp32: acc += s * P (with 64-wide groups, two
+//     partial sums per stage, one per k-block).  This equals sum_k (q * s) * x up to fp32
+//     rounding;
+//   * stages alternate between two MMA issuers and two dequantiser groups by parity: issuer
+//     i issues all eight MMAs of its stages (one accumulator per scale group, one commit),
+//     fed by dequantiser group i.  The issuers never wait on an mbarrier: they poll two
+//     counters in shared memory, "q of stage it written and its tokens landed" (published by
+//     their dequantiser group after a named barrier) and "partial-sum slot released"
+//     (published by the epilogue after a named barrier);
+//   * the q / token ring (kQS stages) and the partial-sum ring (kPS slots) are separate, so
+//     the round trips dequantise -> MMA -> q slot free and MMA -> epilogue read -> partial
+//     slot free each span several stages.
 //
 // CTA = one 128-row weight block x up to 32 tokens of one segment (x one K chunk when
-// split-K is used), streamed in 128-K stages.  Warp roles (544 threads, one CTA per SM):
+// split-K is used), streamed in 128-K stages.  Warp roles (512 threads, one CTA per SM):
 //   warp 0        token producer: two TMA boxes (16 or 32 rows x 64 K) per stage
 //   warp 1        weight producer: one bulk copy of the int4 super-block per stage
-//   warps 2, 3    MMA issuers for k-block 0 / 1 of every stage (tcgen05 "TS": A = q from
-//                 tensor memory, B = tokens from shared memory)
-//   warps 4..11   dequantisers, two groups of four (group g owns ring slots s with
-//                 s % 2 == g), one weight row per thread; they also pass each row's fp16
-//                 scales of the stage to the epilogue through a shared-memory ring of
-//                 2 x kRing slots (a slot is rewritten only after the epilogue has released
-//                 the partial sums of the round before)
+//   warps 2, 3    MMA issuers of the even / odd stages (tcgen05 "TS": A = q from tensor
+//                 memory, B = tokens from shared memory)
+//   warps 4..11   dequantisers, group g = warps 4+4g..7+4g owns the stages of parity g, one
+//                 weight row per thread; it also hands each row's fp16 scales of the stage
+//                 to the epilogue through a shared-memory ring
 //   warps 12..15  epilogue: partial sums -> registers (scaled), output at the tile end
-//   warp 16       waits on the stage-ready barrier for the issuers and publishes a counter
-//                 they poll (an mbarrier wait in an MMA-issuing thread costs ~270 cycles,
-//                 a shared-memory load ~40)
 // Epilogues: SwiGLU (gate rows 0..63 / up rows 64..127 of the paired layout), plain bf16,
 // or fp32 partial sums per K chunk for split-K (reduced in a fixed order by the combine
 // kernel, so results are deterministic).
@@ -61,31 +57,33 @@ namespace {
 
 constexpr int kBM = 128;             // weight rows per tile
 constexpr int kBN = 32;              // tokens per tile (segments with more rows use several)
-constexpr int kDQ = 8;               // dequantiser warps
-constexpr int kGroups = kDQ / 4;
 constexpr int kWST = 16;             // int4 super-block stages (shared memory)
-constexpr int kRing = 4;             // q (tensor memory, 64 columns), token (shared memory) and
-                                     // partial-sum (tensor memory, 2 x kBN columns) stages
-constexpr int kWarpX = 0, kWarpW = 1, kWarpM0 = 2, kWarpDQ = 4, kWarpEpi = kWarpDQ + kDQ;
-constexpr int kWarpSync = kWarpEpi + 4;   // waits on a_full for the issuers
-constexpr int kThreads = (kWarpSync + 1) * 32;
+constexpr int kWarpX = 0, kWarpW = 1, kWarpM0 = 2, kWarpDQ = 4, kWarpEpi = 12;
+constexpr int kThreads = (kWarpEpi + 4) * 32;
 constexpr uint32_t kBStageBytes = 2u * kBN * 64 * 2;          // [2 k-blocks][32 tokens][64] bf16, SW128
 constexpr uint32_t kWStageBytes = kW4SuperInt4Bytes + 512;    // int4 + up to two scale groups
 constexpr uint32_t kXchgBytes = 64 * (kBN + 1) * 4;           // SwiGLU exchange [64 rows][33]
-constexpr uint32_t kScaleBytes = 2 * kRing * 2 * kBM * 4;     // fp32 scales [2 x ring][k-block][row]
-constexpr uint32_t kTmemP = kRing * 64;                       // partial sums after the q stages
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSite = 0x300u;
-static_assert(kTmemP + kRing * 2 * kBN <= kTmemCols, "tensor memory budget");
-static_assert(kWST % kGroups == 0 && kRing % kGroups == 0, "every stage has one owning dequantiser group");
-// Parity waits are exact only while a waiter is at most one phase behind its barrier:
-//   a_full[s]   (warp 16, for the issuers) -- the next round needs the epilogue's release of
-//               this round, which needs this round's MMAs, issued after warp 16 published
-//   mma_done[s] (epilogue) -- the next round's MMAs need the epilogue's release;
-//               (dequantisers, token producer, waiting for the previous round) -- this
-//               round needs their own arrivals
-// The scale ring has 2 x kRing slots: the slot of iteration i is rewritten at i + 2 kRing,
-// after mma_done of i + kRing, whose MMAs waited for the epilogue's release of i.
+constexpr uint32_t kBarEpi = 1, kBarDQ0 = 2;                  // named barriers (kBarDQ0 + group)
+
+__host__ __device__ constexpr int cgcd(int a, int b) { return b == 0 ? a : cgcd(b, a % b); }
+
+// Ring geometry per scale groups per stage (SG = 1: groups of >= 128 K values; SG = 2: 64).
+template <int SG>
+struct Geo {
+  static constexpr int kQS = SG == 1 ? 6 : 4;                 // q (tensor memory) + token stages
+  static constexpr int kPS = 4;                               // partial-sum slots
+  static constexpr int kPCols = SG * kBN;                     // tensor-memory columns per slot
+  static constexpr int kRing = kQS / cgcd(kQS, kPS) * kPS;    // stage_done barriers: lcm(kQS, kPS)
+  static constexpr int kSR = kQS + kPS;                       // scale-ring slots
+  static constexpr uint32_t kTmemP = kQS * 64;                // partial sums after the q stages
+  static constexpr uint32_t kScaleBytes = kSR * SG * kBM * 4;
+  static_assert(kTmemP + kPS * kPCols <= kTmemCols, "tensor memory budget");
+  static_assert(kQS % 2 == 0 && kPS % 2 == 0 && kWST % 2 == 0 && kRing % 2 == 0,
+                "every ring slot belongs to the stages of one parity (one issuer, one dequantiser group)");
+  static_assert(kRing <= 16 && kQS <= 8, "barrier arrays");
+};
 
 struct DecodeArgs {
   const uint8_t* wq;
@@ -103,13 +101,25 @@ struct DecodeArgs {
   uint32_t* err;
 };
 
+// Parity waits are exact only while a waiter is at most one phase behind its barrier:
+//   stage_done[b] (stages b, b + kRing, ...; the issuer's commit + the 4 dequantiser warps'
+//     "scales written"): the epilogue waits for stage it -- stage it + kRing needs the
+//     partial-sum slot the epilogue releases after reading stage it + kRing - kPS >= it;
+//     the dequantisers and the token producer wait for stage it - kQS before reusing its
+//     q / token slot -- stage it - kQS + kRing needs this stage's q and tokens first;
+//   tok_full[s] (dequantisers of stage it): the tokens of it + kQS are only loaded after
+//     stage it is done, which needs the dequantisers' q of stage it first;
+//   w_full / w_empty: a producer / consumer ring with one consumer group per slot.
+// A dequantiser arrival for stage it lands in the phase of stage it: the phase of stage
+// it - kRing (same parity, so the same issuer, committed before stage it - kQS) completed
+// before the dequantisers' wait for stage it - kQS returned.
 struct __align__(8) DecodeBars {
   uint64_t w_full[kWST], w_empty[kWST];
-  uint64_t a_full[kRing];      // q written (4 dequantiser warps), tokens landed (producer +
-                               // bytes), previous round's partial sums read (4 epilogue warps)
-  uint64_t mma_done[kRing];    // both issuers' MMAs finished (2 commits), scales written (4)
+  uint64_t tok_full[8];
+  uint64_t stage_done[16];
   uint64_t done[2];
-  uint32_t ready;              // stages whose a_full phase has completed (published by kWarpSync)
+  uint32_t q_ready[2];         // per parity: it + 1 of the last stage whose q and tokens are ready
+  uint32_t p_rel;              // stages whose partial sums the epilogue has read
   uint32_t tmem_base;
   int abort;
   int total_tiles;
@@ -118,9 +128,12 @@ struct __align__(8) DecodeBars {
   int seg_w[kMaxGemmExperts];
 };
 
-constexpr uint32_t kSmemBytes =
-    1024 + kRing * kBStageBytes + kWST * kWStageBytes + kXchgBytes + kScaleBytes + sizeof(DecodeBars);
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+template <int SG>
+constexpr uint32_t decode_smem_bytes() {
+  return 1024 + Geo<SG>::kQS * kBStageBytes + kWST * kWStageBytes + kXchgBytes + Geo<SG>::kScaleBytes +
+         (uint32_t)sizeof(DecodeBars);
+}
+static_assert(decode_smem_bytes<1>() <= 232448 && decode_smem_bytes<2>() <= 232448, "shared memory budget");
 
 struct DTile {
   int e, w, fb, kc, row0, rows;
@@ -167,16 +180,18 @@ __device__ __forceinline__ void dequant_q_half(const uint4 v, const __nv_bfloat1
 
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+template <int SG>
 __global__ void __launch_bounds__(kThreads, 1)
     w4_decode_kernel(const __grid_constant__ CUtensorMap tm_x16, const __grid_constant__ CUtensorMap tm_x32,
                      const DecodeArgs a) {
+  using G = Geo<SG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* b_stages = base;                                  // kRing x [2][32][64] bf16 (SW128)
-  uint8_t* w_stages = b_stages + kRing * kBStageBytes;       // kWST x int4 super-block
+  uint8_t* b_stages = base;                                  // kQS x [2][32][64] bf16 (SW128)
+  uint8_t* w_stages = b_stages + G::kQS * kBStageBytes;      // kWST x int4 super-block
   float* xchg = reinterpret_cast<float*>(w_stages + kWST * kWStageBytes);
-  float* scl = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xchg) + kXchgBytes);   // [2 kRing][2][128]
-  DecodeBars* bars = reinterpret_cast<DecodeBars*>(reinterpret_cast<uint8_t*>(scl) + kScaleBytes);
+  float* scl = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xchg) + kXchgBytes);   // [kSR][SG][128]
+  DecodeBars* bars = reinterpret_cast<DecodeBars*>(reinterpret_cast<uint8_t*>(scl) + G::kScaleBytes);
   volatile int* abort_flag = &bars->abort;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -187,18 +202,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->w_full[s], 1);
       mbar_init(&bars->w_empty[s], 4);    // the four warps of the owning dequantiser group
     }
-    for (int s = 0; s < kRing; ++s) {
-      mbar_init(&bars->a_full[s], 4 + 1 + 4);
-      mbar_init(&bars->mma_done[s], 2 + 4);
-    }
+    for (int s = 0; s < G::kQS; ++s) mbar_init(&bars->tok_full[s], 1);
+    for (int s = 0; s < G::kRing; ++s) mbar_init(&bars->stage_done[s], 1 + 4);   // commit + scales written
     mbar_init(&bars->done[0], 1);
     mbar_init(&bars->done[1], 1);
     bars->abort = 0;
-    bars->ready = 0;
+    bars->q_ready[0] = 0;
+    bars->q_ready[1] = 0;
+    bars->p_rel = 0;
     fence_mbar_init();
-    // the epilogue's share of every slot's first round: there is no earlier round to release
-    for (int s = 0; s < kRing; ++s)
-      for (int i = 0; i < 4; ++i) mbar_arrive(&bars->a_full[s]);
   }
   if (warp == kWarpX && lane == 0) {
     tma_prefetch_desc(&tm_x16);
@@ -250,22 +262,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* tm = box == 16 ? &tm_x16 : &tm_x32;
         const uint32_t bytes = (uint32_t)(2 * box * 128);
         for (int ks = 0; ks < ks_per; ++ks, ++it) {
-          const int s = it % kRing;
-          if (!mbar_wait(&bars->mma_done[s], ((it / kRing) & 1u) ^ 1u, a.err, abort_flag, kSite + 1)) {
-            ok = false;
-            break;
+          const int s = it % G::kQS;
+          // the slot's previous tokens (stage it - kQS) have been read by their MMAs
+          if (it >= (uint32_t)G::kQS) {
+            const uint32_t j = it - G::kQS;
+            if (!mbar_wait(&bars->stage_done[j % G::kRing], (j / G::kRing) & 1u, a.err, abort_flag, kSite + 1)) {
+              ok = false;
+              break;
+            }
           }
           uint8_t* bsm = b_stages + s * kBStageBytes;
           const int kglob = (t.kc * ks_per + ks) * kW4SuperK;
-          mbar_arrive_expect_tx(&bars->a_full[s], bytes);
-          tma_load_2d(bsm, tm, &bars->a_full[s], kglob, t.row0);
-          tma_load_2d(bsm + kBN * 128, tm, &bars->a_full[s], kglob + 64, t.row0);
+          mbar_arrive_expect_tx(&bars->tok_full[s], bytes);
+          tma_load_2d(bsm, tm, &bars->tok_full[s], kglob, t.row0);
+          tma_load_2d(bsm + kBN * 128, tm, &bars->tok_full[s], kglob + 64, t.row0);
         }
       }
-      // no copy of this CTA may still be in flight when it exits (the phase also needs the
-      // other arrivals, which a run without errors always makes)
-      const uint32_t first = it > (uint32_t)kRing ? it - kRing : 0u;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->a_full[j % kRing], (j / kRing) & 1u, a.err, nullptr, kSite + 2);
+      // no copy of this CTA may still be in flight when it exits
+      const uint32_t first = it > (uint32_t)G::kQS ? it - G::kQS : 0u;
+      for (uint32_t j = first; j < it; ++j)
+        mbar_wait(&bars->tok_full[j % G::kQS], (j / G::kQS) & 1u, a.err, nullptr, kSite + 2);
     }
   } else if (warp == kWarpW) {
     // ------------------------------------------------------------------ weight producer
@@ -287,11 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const uint32_t first = it > (uint32_t)kWST ? it - kWST : 0u;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&bars->w_full[j % kWST], (j / kWST) & 1u, a.err, nullptr, kSite + 4);
+      for (uint32_t j = first; j < it; ++j)
+        mbar_wait(&bars->w_full[j % kWST], (j / kWST) & 1u, a.err, nullptr, kSite + 4);
     }
   } else if (warp < kWarpDQ) {
     // ------------------------------------------------------------------ MMA issuers
-    const int kb = warp - kWarpM0;   // the k-block of every stage this warp issues
+    const uint32_t par = (uint32_t)(warp - kWarpM0);   // this issuer's stage parity
     if (lane == 0) {
       uint32_t it = 0;
       int e_hint = 0;
@@ -300,38 +317,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const DTile t = dtile_at(bars, tile, e_hint, a.ksplit);
         const uint32_t idesc = idesc_bf16_f32(kBM, (uint32_t)((t.rows + 15) & ~15));
         for (int ks = 0; ks < ks_per; ++ks, ++it) {
-          const int s = it % kRing;
-          if (!counter_wait(&bars->ready, it, a.err, abort_flag, kSite + 5)) {
+          if ((it & 1u) != par) continue;
+          const int sq = it % G::kQS, sp = it % G::kPS;
+          // q and tokens of this stage are ready, and the partial sums of stage it - kPS
+          // (the slot's previous use) have been read
+          bool ready = counter_wait(&bars->q_ready[par], it, a.err, abort_flag, kSite + 5);
+          if (ready && it >= (uint32_t)G::kPS)
+            ready = counter_wait(&bars->p_rel, it - G::kPS, a.err, abort_flag, kSite + 6);
+          if (!ready) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem + kTmemP + (uint32_t)(2 * s + kb) * kBN;
-          const uint32_t a_tmem = tmem + (uint32_t)s * 64 + (uint32_t)kb * 32;
-          const uint64_t bdesc = sdesc_k_sw128(smem_u32(b_stages + s * kBStageBytes) + kb * kBN * 128);
+          const uint32_t d_tmem = tmem + G::kTmemP + (uint32_t)sp * G::kPCols;
+          const uint32_t a_tmem = tmem + (uint32_t)sq * 64;
+          const uint32_t bsm = smem_u32(b_stages + sq * kBStageBytes);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)   // +32 bytes along K = +2 in the descriptor's address field
-            mma_ts(d_tmem, a_tmem + kk * 8, bdesc + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : 0u);
-          mma_commit(&bars->mma_done[s]);   // frees the q and token stages, publishes the partial sums
-        }
-      }
-      mma_commit(&bars->done[kb]);
-      mbar_wait(&bars->done[kb], 0, a.err, nullptr, kSite + 8);
-    }
-  } else if (warp == kWarpSync) {
-    // ------------------------------------------------------------------ issuers' waiter
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        for (int ks = 0; ks < ks_per; ++ks, ++it) {
-          if (!mbar_wait(&bars->a_full[it % kRing], (it / kRing) & 1u, a.err, abort_flag, kSite + 14)) {
-            ok = false;
-            break;
+          for (int kb = 0; kb < 2; ++kb) {
+            const uint64_t bdesc = sdesc_k_sw128(bsm + kb * kBN * 128);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {   // +32 bytes along K = +2 in the descriptor's address field
+              const uint32_t accum = SG == 2 ? (kk > 0 ? 1u : 0u) : ((kb | kk) != 0 ? 1u : 0u);
+              mma_ts(d_tmem + (SG == 2 ? (uint32_t)kb * kBN : 0u), a_tmem + kb * 32 + kk * 8,
+                     bdesc + (uint64_t)(2 * kk), idesc, accum);
+            }
           }
-          st_release_shared(&bars->ready, it + 1);
+          mma_commit(&bars->stage_done[it % G::kRing]);   // frees q / tokens, publishes the partial sums
         }
       }
+      mma_commit(&bars->done[par]);
+      mbar_wait(&bars->done[par], 0, a.err, nullptr, kSite + 8);
     }
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------------ dequantisers
@@ -339,103 +354,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;          // tensor-memory lane quarter this warp may access
     const int row = q * 32 + lane;   // weight row within the tile
     const __nv_bfloat162 off136 = __floats2bfloat162_rn(136.0f, 136.0f);
-    const int s1_idx = w4_scale_groups(a.group_size) > 1 ? kBM : 0;   // k-block 1: next group when g == 64
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       for (int ks = 0; ks < ks_per; ++ks, ++it) {
-        const int s = it % kRing;
-        if (s % kGroups != grp) continue;
-        const uint32_t ph = (it / kRing) & 1u;
+        if ((int)(it & 1u) != grp) continue;
+        const int sq = it % G::kQS;
         const int sw = it % kWST;
-        if (!mbar_wait(&bars->w_full[sw], (it / kWST) & 1u, a.err, abort_flag, kSite + 10)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* wsm = w_stages + sw * kWStageBytes;
+        bool fail = !mbar_wait(&bars->w_full[sw], (it / kWST) & 1u, a.err, abort_flag, kSite + 10);
         uint4 v[4];
+        float s0 = 0.f, s1 = 0.f;
+        if (!fail) {
+          const uint8_t* wsm = w_stages + sw * kWStageBytes;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4*>(wsm + i * 2048 + row * 16);
-        const uint16_t* ssm = reinterpret_cast<const uint16_t*>(wsm + kW4SuperInt4Bytes);
-        const float s0 = __half2float(__ushort_as_half(ssm[row]));
-        const float s1 = __half2float(__ushort_as_half(ssm[s1_idx + row]));
+          for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4*>(wsm + i * 2048 + row * 16);
+          const uint16_t* ssm = reinterpret_cast<const uint16_t*>(wsm + kW4SuperInt4Bytes);
+          s0 = __half2float(__ushort_as_half(ssm[row]));
+          if (SG == 2) s1 = __half2float(__ushort_as_half(ssm[kBM + row]));
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->w_empty[sw]);
-        // the q stage is free once the MMAs of the previous round of this slot are done
-        if (!mbar_wait(&bars->mma_done[s], ph ^ 1u, a.err, abort_flag, kSite + 11)) {
-          ok = false;
-          break;
+        if (!fail && lane == 0) mbar_arrive(&bars->w_empty[sw]);
+        // the q slot is free once the MMAs of stage it - kQS are done
+        if (!fail && it >= (uint32_t)G::kQS) {
+          const uint32_t j = it - G::kQS;
+          fail = !mbar_wait(&bars->stage_done[j % G::kRing], (j / G::kRing) & 1u, a.err, abort_flag, kSite + 11);
         }
-        tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)s * 64;
+        if (!fail) {
+          tc_fence_after();
+          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)sq * 64;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t o[16];
-          dequant_q_half(v[i], off136, o);
-          tmem_st16(taddr + i * 16, o);
+          for (int i = 0; i < 4; ++i) {
+            uint32_t o[16];
+            dequant_q_half(v[i], off136, o);
+            tmem_st16(taddr + i * 16, o);
+          }
+          tmem_wait_st();
+          float* sc = scl + (it % G::kSR) * SG * kBM;
+          sc[row] = s0;
+          if (SG == 2) sc[kBM + row] = s1;
+          fail = !mbar_wait(&bars->tok_full[sq], (it / G::kQS) & 1u, a.err, abort_flag, kSite + 12);
         }
-        tmem_wait_st();
-        const int ss = it % (2 * kRing);
-        scl[(2 * ss) * kBM + row] = s0;
-        scl[(2 * ss + 1) * kBM + row] = s1;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bars->mma_done[s]);   // scales of this round written
-          mbar_arrive(&bars->a_full[s]);     // q of this round written
+        if (!fail && lane == 0) mbar_arrive(&bars->stage_done[it % G::kRing]);   // scales of this stage written
+        // the group's four warps agree; then one thread publishes the stage to its issuer
+        if (named_bar_any(kBarDQ0 + grp, 128, fail)) {
+          ok = false;
+          break;
         }
+        if (q == 0 && lane == 0) st_release_shared(&bars->q_ready[grp], it + 1);
       }
     }
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + kTmemP;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::kTmemP;
     uint32_t it = 0;
     int e_hint = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       const DTile t = dtile_at(bars, tile, e_hint, a.ksplit);
       const int n_eff = (t.rows + 15) & ~15;
-      bool ok = true;
       float acc[kBN];
 #pragma unroll
       for (int j = 0; j < kBN; ++j) acc[j] = 0.f;
       for (int ks = 0; ks < ks_per; ++ks, ++it) {
-        const int s = it % kRing, sp = 2 * s, ss = it % (2 * kRing);
-        if (!mbar_wait(&bars->mma_done[s], (it / kRing) & 1u, a.err, abort_flag, kSite + 12)) {
+        const int sp = it % G::kPS;
+        const bool fail =
+            !mbar_wait(&bars->stage_done[it % G::kRing], (it / G::kRing) & 1u, a.err, abort_flag, kSite + 13);
+        // group 0 (or the only group): columns 0-15 / 16-31; group 1 (64-wide groups) likewise
+        uint32_t a0[16], a1[16], b0[16], b1[16];
+        float s0 = 0.f, s1 = 0.f;
+        if (!fail) {
+          tc_fence_after();
+          const float* sc = scl + (it % G::kSR) * SG * kBM;
+          s0 = sc[row];
+          if (SG == 2) s1 = sc[kBM + row];
+          const uint32_t pa = lane_base + (uint32_t)sp * G::kPCols;
+          if (n_eff > 16) {
+            tmem_ld16x2(pa, pa + 16, a0, a1);
+            if (SG == 2) tmem_ld16x2(pa + kBN, pa + kBN + 16, b0, b1);
+          } else if (SG == 2) {
+            tmem_ld16x2(pa, pa + kBN, a0, b0);
+          } else {
+            tmem_ld16(pa, a0);
+          }
+          tc_fence_before();
+        }
+        // the four warps have read the slot: release it to the issuers
+        if (named_bar_any(kBarEpi, 128, fail)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const float s0 = scl[(2 * ss) * kBM + row];
-        const float s1 = scl[(2 * ss + 1) * kBM + row];
-        // both k-blocks' partial sums, 16 columns at a time; the slot is released as soon as
-        // the last columns are in registers
+        if (q == 0 && lane == 0) st_release_shared(&bars->p_rel, it + 1);
 #pragma unroll
-        for (int c0 = 0; c0 < kBN; c0 += 16) {
-          if (c0 < n_eff) {
-            uint32_t p0[16], p1[16];
-            tmem_ld16x2(lane_base + (uint32_t)sp * kBN + c0, lane_base + (uint32_t)(sp + 1) * kBN + c0, p0, p1);
-            if (c0 + 16 >= n_eff) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&bars->a_full[s]);   // counts toward the slot's next round
-            }
+        for (int j = 0; j < 16; ++j) {
+          acc[j] = __fmaf_rn(s0, __uint_as_float(a0[j]), acc[j]);
+          if (SG == 2) acc[j] = __fmaf_rn(s1, __uint_as_float(b0[j]), acc[j]);
+        }
+        if (n_eff > 16) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              acc[c0 + j] = __fmaf_rn(s1, __uint_as_float(p1[j]), __fmaf_rn(s0, __uint_as_float(p0[j]), acc[c0 + j]));
+          for (int j = 0; j < 16; ++j) {
+            acc[16 + j] = __fmaf_rn(s0, __uint_as_float(a1[j]), acc[16 + j]);
+            if (SG == 2) acc[16 + j] = __fmaf_rn(s1, __uint_as_float(b1[j]), acc[16 + j]);
           }
         }
       }
+      if (!ok) break;
       // ---------------------------------------------------------------- output
       // thread = weight row, acc[j] = token row0 + j; every epilogue warp takes every barrier
       if (a.mode == kDecodeSwiGLU) {
-        if (ok && q >= 2) {
+        if (q >= 2) {
 #pragma unroll
           for (int j = 0; j < kBN; ++j) xchg[(row - 64) * (kBN + 1) + j] = acc[j];
         }
-        named_bar_sync(1, 128);
-        if (ok && q < 2) {
+        named_bar_sync(kBarEpi, 128);
+        if (q < 2) {
           __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
 #pragma unroll
           for (int j = 0; j < kBN; ++j)
@@ -443,19 +478,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               out[(int64_t)(t.row0 + j) * a.ldo + t.fb * 64 + row] =
                   __float2bfloat16_rn(silu_f(acc[j]) * xchg[row * (kBN + 1) + j]);
         }
-      } else if (ok && a.mode == kDecodePlain) {
+        named_bar_sync(kBarEpi, 128);   // xchg is free for the next tile
+      } else if (a.mode == kDecodePlain) {
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
 #pragma unroll
         for (int j = 0; j < kBN; ++j)
           if (j < t.rows) out[(int64_t)(t.row0 + j) * a.ldo + t.fb * kBM + row] = __float2bfloat16_rn(acc[j]);
-      } else if (ok) {   // fp32 partial sums of K chunk kc
+      } else {   // fp32 partial sums of K chunk kc
         float* out = static_cast<float*>(a.out) + (int64_t)t.kc * a.R * a.ldo;
 #pragma unroll
         for (int j = 0; j < kBN; ++j)
           if (j < t.rows) out[(int64_t)(t.row0 + j) * a.ldo + t.fb * kBM + row] = acc[j];
       }
-      // xchg is free for the next tile; the four warps leave together after a failure
-      if (named_bar_any(1, 128, !ok)) break;
     }
   }
 
@@ -465,6 +499,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+template <int SG>
+int launch_decode(const CUtensorMap& tm16, const CUtensorMap& tm32, const DecodeArgs& a, int grid,
+                  cudaStream_t stream) {
+  constexpr uint32_t smem = decode_smem_bytes<SG>();
+  auto fn = w4_decode_kernel<SG>;
+  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+  if (st != LMOE_OK) return st;
+  fn<<<grid, kThreads, smem, stream>>>(tm16, tm32, a);
+  return cuda_status(cudaGetLastError());
 }
 
 }  // namespace
@@ -511,12 +556,8 @@ int run_decode_gemm(const DecodeProblem& p, cudaStream_t stream) {
   st = encode_tmap_2d(&tm_x32, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,
                       (uint64_t)p.ldx * 2, 32, 64, true);
   if (st != LMOE_OK) return st;
-  {
-    const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(w4_decode_kernel), kSmemBytes);
-    if (st != LMOE_OK) return st;
-  }
-  w4_decode_kernel<<<dev.num_sms, kThreads, kSmemBytes, stream>>>(tm_x16, tm_x32, a);
-  return cuda_status(cudaGetLastError());
+  if (w4_scale_groups(g) == 2) return launch_decode<2>(tm_x16, tm_x32, a, dev.num_sms, stream);
+  return launch_decode<1>(tm_x16, tm_x32, a, dev.num_sms, stream);
 }
 
 }  // namespace lmoe

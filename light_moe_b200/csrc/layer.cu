@@ -197,39 +197,61 @@ __global__ void combine_rows_kernel(const __nv_bfloat162* __restrict__ rows, con
 }
 
 // Decode path: y[t, :] = sum_j w[t*k+j] * P(pos[t*k+j]) + sum_s P(Rr + s*T + t), where
-// P(r) = sum over the K chunks c of part[c][r, :] (fp32, chunk order fixed).
-__global__ void combine_partials_kernel(const float* __restrict__ part, int ksplit, int64_t R,
+// P(r) = sum over the K chunks c of part[c][r, :] (fp32, chunk order fixed).  Four columns per
+// thread (16-byte loads; d % 4 == 0).
+__global__ void combine_partials_kernel(const float4* __restrict__ part, int ksplit, int64_t R,
                                         const int32_t* __restrict__ pos, const float* __restrict__ w, int64_t T,
-                                        int k, int S, int d, __nv_bfloat16* __restrict__ y) {
+                                        int k, int S, int d4, uint2* __restrict__ y) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= T * d) return;
-  const int64_t t = i / d;
-  const int c = (int)(i - t * d);
+  if (i >= T * d4) return;
+  const int64_t t = i / d4;
+  const int c = (int)(i - t * d4);
   const int64_t Rr = T * k;
-  float acc = 0.0f;
-  for (int j = 0; j < k; ++j) {
-    const int64_t r = pos[t * k + j];
-    float v = 0.0f;
-    for (int q = 0; q < ksplit; ++q) v = __fadd_rn(v, part[((int64_t)q * R + r) * d + c]);
-    acc = __fadd_rn(acc, __fmul_rn(w[t * k + j], v));
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < k + S; ++j) {
+    const int64_t r = j < k ? (int64_t)pos[t * k + j] : Rr + (int64_t)(j - k) * T + t;
+    const float wj = j < k ? w[t * k + j] : 1.0f;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < ksplit; ++q) {
+      const float4 p = __ldcs(part + ((int64_t)q * R + r) * d4 + c);
+      v.x = __fadd_rn(v.x, p.x);
+      v.y = __fadd_rn(v.y, p.y);
+      v.z = __fadd_rn(v.z, p.z);
+      v.w = __fadd_rn(v.w, p.w);
+    }
+    if (j < k) {
+      acc.x = __fadd_rn(acc.x, __fmul_rn(wj, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(wj, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(wj, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(wj, v.w));
+    } else {
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
   }
-  for (int s2 = 0; s2 < S; ++s2) {
-    const int64_t r = Rr + (int64_t)s2 * T + t;
-    float v = 0.0f;
-    for (int q = 0; q < ksplit; ++q) v = __fadd_rn(v, part[((int64_t)q * R + r) * d + c]);
-    acc = __fadd_rn(acc, v);
-  }
-  y[i] = __float2bfloat16_rn(acc);
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+  y[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
 }
 
-// K chunks for the decode down projection: the smallest divisor of the stage count that gives
-// at least ~8 tiles per SM, so the tail of the static schedule stays short.
-inline int pick_ksplit(int KS, int64_t tiles_per_chunk, int num_sms) {
-  for (int d = 1; d <= KS && d <= 16; ++d)
-    if (KS % d == 0 && tiles_per_chunk * d >= 8LL * num_sms) return d;
+// K chunks for the decode down projection: the divisor d of the stage count KS (d <= 16)
+// that minimises the modelled time in stage units per SM: the static schedule's makespan,
+// ceil(tiles * d / SMs) tiles of KS / d stages, plus the fp32 partial sums written and read
+// back by the combine (d * rows * N * 8 bytes spread over the SMs, at one stage per
+// stage_bytes).
+inline int pick_ksplit(int KS, int64_t tiles_per_chunk, int num_sms, int64_t rows, int64_t N, int64_t stage_bytes) {
   int best = 1;
-  for (int d = 1; d <= KS && d <= 16; ++d)
-    if (KS % d == 0) best = d;
+  double best_cost = 1e300;
+  for (int d = 1; d <= KS && d <= 16; ++d) {
+    if (KS % d) continue;
+    const double waves = (double)((tiles_per_chunk * d + num_sms - 1) / num_sms);
+    const double cost = waves * (KS / d) + (double)d * rows * N * 8.0 / num_sms / (double)stage_bytes;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = d;
+    }
+  }
   return best;
 }
 
@@ -455,6 +477,7 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
   LMOE_ARG_CHECK(d % 128 == 0 && F % 128 == 0 && group_size % 64 == 0 && d % group_size == 0 && F % group_size == 0);
   LMOE_ARG_CHECK(group_size >= kW4SuperK || kW4SuperK % group_size == 0);
   LMOE_ARG_CHECK(x && gate_weight && w13_packed && w2_packed && y);
+  LMOE_ARG_CHECK((reinterpret_cast<uintptr_t>(y) & 7) == 0);
   const LayerWs L = layer_ws(T, d, F, E, k, S);
   if (!workspace || workspace_bytes < L.total || !aligned16(workspace)) return LMOE_ERR_WORKSPACE;
   if (T == 0) return LMOE_OK;
@@ -511,7 +534,8 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
     st = get_device_info(&dev);
     if (st != LMOE_OK) return st;
     const int KS2 = F / kW4SuperK;
-    const int ksplit = pick_ksplit(KS2, (int64_t)(E + S) * (d / 128), dev.num_sms);
+    // decode tiles: every segment holds at most T <= 64 rows, i.e. at most two 32-row tiles
+    const int ksplit = pick_ksplit(KS2, (int64_t)(E + S) * (d / 128), dev.num_sms, R, d, w4_super_bytes(group_size));
     DecodeProblem d2 = d1;
     d2.x = at(L.h);
     d2.ldx = F;
@@ -525,9 +549,9 @@ extern "C" int lmoe_moe_layer_w4a16(const void* x, int64_t num_tokens, int hidde
     st = run_decode_gemm(d2, stream);
     if (st != LMOE_OK) return st;
     const int threads = 256;
-    const int64_t n = T * d;
+    const int64_t n = T * (d / 4);
     combine_partials_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
-        static_cast<const float*>(at(L.part)), ksplit, R, posn, wts, T, k, S, d, static_cast<__nv_bfloat16*>(y));
+        static_cast<const float4*>(at(L.part)), ksplit, R, posn, wts, T, k, S, d / 4, static_cast<uint2*>(y));
     return cuda_status(cudaGetLastError());
   }
   // a routed expert receives at most T rows; shared experts exactly T

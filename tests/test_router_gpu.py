@@ -86,6 +86,16 @@ def test_router_full_size(E, k):
     out = router(x, w, k)
     _check_given_logits(out, k, E)
     assert out["offsets"][-1] == 16384 * k
+    # end to end against fp64 logits of the same inputs: every token whose k-th / (k+1)-th
+    # gap exceeds twice the fp32 accumulation bound selects exactly the oracle's experts
+    lg64 = oracle.gate_logits_f64(x.float().cpu().numpy(), w.float().cpu().numpy())
+    bound = _logit_bound(x, w)
+    assert np.all(np.abs(out["logits"] - lg64) <= bound)
+    ids_ref, _ = oracle.route(lg64.astype(np.float32), k)
+    srt = np.sort(lg64, axis=1)[:, ::-1]
+    safe = srt[:, k - 1] - srt[:, k] > 2 * bound.max(axis=1)
+    assert safe.mean() > 0.99, safe.mean()
+    assert np.array_equal(np.sort(out["ids"][safe], 1), np.sort(ids_ref[safe], 1))
 
 
 def test_router_ties_go_to_lower_expert_id():

@@ -208,3 +208,54 @@ def test_reference_grouped_gemm_op():
     off = torch.tensor([0, 10, 10, 60, 90], dtype=torch.int64, device="cuda")
     y = ops.grouped_gemm(x, w, off, E)
     _assert_close(y, _ref_plain(x, w.float(), off))
+
+
+def test_mixtral_grouped_gemms_zipf_full_shape():
+    """The Mixtral grouped GEMMs at full shape with a Zipf(1.2) expert load over 8192 rows
+    (3516 ... 289 rows per expert, the skewed-GEMM workload): gate/up + SwiGLU, then down,
+    checked against fp32 math on the dequantised weights for 48 rows of every segment
+    (its first, last and evenly spaced rows), h of the kernel feeding the down reference."""
+    E, d, F, g, R = 8, 4096, 14336, 128, 8192
+    p = [(i + 1) ** -1.2 for i in range(E)]
+    cnt = [int(R * v / sum(p)) for v in p]
+    cnt[0] += R - sum(cnt)
+    off = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
+    gen = torch.Generator(device="cpu").manual_seed(12)
+    x = torch.randn(R, d, generator=gen).to(torch.bfloat16).cuda()
+    dev = torch.device("cuda")
+    q1s, s1s, q3s, s3s, q2s, s2s = [], [], [], [], [], []
+    for e in range(E):
+        for qs, ss, shape in ((q1s, s1s, (F, d)), (q3s, s3s, (F, d)), (q2s, s2s, (d, F))):
+            w = (torch.randn(*shape, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+            q, s = quantize(w, g)
+            qs.append(q)
+            ss.append(s)
+    st = torch.stack
+    w13 = prepack(st(q1s), st(s1s), g, st(q3s), st(s3s))
+    w2 = prepack(st(q2s), st(s2s), g)
+    offsets = torch.from_numpy(off).cuda()
+    h = w4_gemm(x, w13, 2 * F, g, offsets, epilogue=1, hint=max(cnt))
+    y = w4_gemm(h, w2, d, g, offsets, epilogue=0, hint=max(cnt))
+    rows = []
+    for e in range(E):
+        a, b = int(off[e]), int(off[e + 1])
+        rows.extend(np.unique(np.linspace(a, b - 1, 48).astype(np.int64)).tolist())
+    idx = torch.tensor(rows, device=dev)
+    hs = torch.empty(len(rows), F, device=dev)
+    ys = torch.empty(len(rows), d, device=dev)
+    for e in range(E):
+        sel = [(i, r) for i, r in enumerate(rows) if off[e] <= r < off[e + 1]]
+        ii = torch.tensor([i for i, _ in sel], device=dev)
+        rr = idx[ii]
+        d1 = dequantize(q1s[e], s1s[e], g).float()
+        d3 = dequantize(q3s[e], s3s[e], g).float()
+        xe = x[rr].float()
+        hs[ii] = torch.nn.functional.silu(xe @ d1.T) * (xe @ d3.T)
+        del d1, d3
+        d2 = dequantize(q2s[e], s2s[e], g).float()
+        ys[ii] = h[rr].float() @ d2.T
+        del d2
+    for got, ref in ((h[idx].float(), hs), (y[idx].float(), ys)):
+        err = (got - ref).abs().max().item()
+        scale = ref.abs().max().item()
+        assert err <= 1e-2 * scale, f"max rel err {err / scale:.3e}"
