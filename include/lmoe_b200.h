@@ -89,14 +89,18 @@ int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight, const floa
  *     accumulation);
  *   - otherwise (fp32 on either side, or bf16 with fp16): fp32 logits on CUDA cores from the
  *     caller's values, each a sequential fp32 sum over the hidden dimension.
- * Workspace: lmoe_router_workspace_bytes_typed().  Everything else as lmoe_fused_gate_topk. */
+ * probs (optional, fp32 [num_tokens, num_experts]) receives the full softmax probabilities,
+ * the router_probs of the reference's RoutingOutput (python/light_moe/ops/moe_gate.py:20-36)
+ * used by its load-balancing loss (:80-122); bit-identical to the values the top-k selects
+ * from.  Workspace: lmoe_router_workspace_bytes_typed().  Everything else as
+ * lmoe_fused_gate_topk. */
 size_t lmoe_router_workspace_bytes_typed(int64_t num_tokens, int num_experts, int x_dtype, int w_dtype);
 
 int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const void* gate_weight, int w_dtype,
                                const float* gate_bias, int64_t num_tokens, int hidden_size, int num_experts,
                                int top_k, int32_t* ids, float* weights, void* weights_bf16,
                                int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
-                               int32_t* positions, float* logits,
+                               int32_t* positions, float* logits, float* probs,
                                void* workspace, size_t workspace_bytes, lmoe_stream_t stream);
 
 /* lmoe_fused_gate_topk without a workspace argument (no counterpart in the reference): the

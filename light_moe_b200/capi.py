@@ -36,7 +36,7 @@ SIGNATURES = {
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),
     "lmoe_fused_gate_topk_typed": (_I, [_P, _I, _P, _I, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                        _SZ, _P]),
+                                        _P, _SZ, _P]),
     "lmoe_fused_gate_topk": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "lmoe_fused_gate_topk_static": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lmoe_permute_rows": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P]),

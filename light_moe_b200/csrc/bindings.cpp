@@ -54,11 +54,12 @@ torch::Tensor workspace(int64_t bytes, const torch::Tensor& like) {
 }
 
 struct Routed {
-  torch::Tensor ids, weights, counts, offsets, sorted_idx, positions, logits;
+  torch::Tensor ids, weights, counts, offsets, sorted_idx, positions, logits, probs;
 };
 
 Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weight,
-             const std::optional<torch::Tensor>& bias, int64_t top_k, bool perm, bool want_logits) {
+             const std::optional<torch::Tensor>& bias, int64_t top_k, bool perm, bool want_logits,
+             bool want_probs = false) {
   check_cuda(hidden_states, "hidden_states");
   check_cuda(gate_weight, "gate_weight");
   TORCH_CHECK(hidden_states.dim() == 2 && gate_weight.dim() == 2, "hidden_states [T,d] and gate_weight [E,d]");
@@ -86,6 +87,7 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
     r.positions = torch::empty({T * top_k}, i32);
   }
   if (want_logits) r.logits = torch::empty({T, E}, x.options().dtype(torch::kFloat32));
+  if (want_probs) r.probs = torch::empty({T, E}, x.options().dtype(torch::kFloat32));
   const int xdt = dtype_code(x), wdt = dtype_code(w);
   auto ws = workspace((int64_t)lmoe_router_workspace_bytes_typed(T, (int)E, xdt, wdt), x);
   int st = lmoe_fused_gate_topk_typed(x.data_ptr(), xdt, w.data_ptr(), wdt, b.defined() ? b.data_ptr<float>() : nullptr,
@@ -95,7 +97,8 @@ Routed route(const torch::Tensor& hidden_states, const torch::Tensor& gate_weigh
                                 perm ? r.offsets.data_ptr<int32_t>() : nullptr,
                                 perm ? r.sorted_idx.data_ptr<int32_t>() : nullptr,
                                 perm ? r.positions.data_ptr<int32_t>() : nullptr,
-                                want_logits ? r.logits.data_ptr<float>() : nullptr, ws.data_ptr(), ws.numel(),
+                                want_logits ? r.logits.data_ptr<float>() : nullptr,
+                                want_probs ? r.probs.data_ptr<float>() : nullptr, ws.data_ptr(), ws.numel(),
                                 cur_stream());
   check_status(st, "fused_gate_topk");
   return r;
@@ -163,10 +166,12 @@ torch::Tensor grouped_gemm(torch::Tensor input, torch::Tensor weights, torch::Te
 // ---------------------------------------------------------------- new ops
 
 std::vector<torch::Tensor> fused_gate_topk_ex(torch::Tensor hidden_states, torch::Tensor gate_weight, int64_t top_k,
-                                              std::optional<torch::Tensor> bias, bool return_logits) {
-  Routed r = route(hidden_states, gate_weight, bias, top_k, true, return_logits);
+                                              std::optional<torch::Tensor> bias, bool return_logits,
+                                              bool return_probs) {
+  Routed r = route(hidden_states, gate_weight, bias, top_k, true, return_logits, return_probs);
   std::vector<torch::Tensor> out = {r.ids, r.weights, r.counts, r.offsets, r.sorted_idx, r.positions};
   if (return_logits) out.push_back(r.logits);
+  if (return_probs) out.push_back(r.probs);
   return out;
 }
 
@@ -323,8 +328,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Gate + top-k + counts/offsets/stable permutation + row gather", py::arg("hidden_states"),
         py::arg("gate_weight"), py::arg("top_k"));
   m.def("fused_gate_topk_ex", &fused_gate_topk_ex,
-        "Router with fp32 weights, int32 counts/offsets/sorted_idx and optional logits", py::arg("hidden_states"),
-        py::arg("gate_weight"), py::arg("top_k"), py::arg("bias") = py::none(), py::arg("return_logits") = false);
+        "Router with fp32 weights, int32 counts/offsets/sorted_idx and optional logits / probabilities",
+        py::arg("hidden_states"), py::arg("gate_weight"), py::arg("top_k"), py::arg("bias") = py::none(),
+        py::arg("return_logits") = false, py::arg("return_probs") = false);
   m.def("quantize_w4", &quantize_w4, "Symmetric per-group int4 quantisation", py::arg("w"), py::arg("group_size"));
   m.def("dequantize_w4", &dequantize_w4, "int4 -> bf16", py::arg("qweight"), py::arg("scales"),
         py::arg("group_size"));

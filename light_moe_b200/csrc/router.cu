@@ -52,6 +52,7 @@ struct RouterArgs {
   float* weights;
   __nv_bfloat16* weights_bf16;
   float* logits;
+  float* probs;           // optional full softmax probabilities [T, E]
   int32_t* counts;
   int32_t* offsets;
   int32_t* sorted_idx;
@@ -428,7 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int e = c0 + i;
-          if (e < a.E) topk_insert<KMAX>(tv, ti, __fmul_rn(__uint_as_float(r[i]), inv), e);
+          if (e < a.E) {
+            const float p = __fmul_rn(__uint_as_float(r[i]), inv);
+            if (a.probs && valid) a.probs[t * a.E + e] = p;
+            topk_insert<KMAX>(tv, ti, p, e);
+          }
         }
       }
       if (split) {
@@ -665,7 +670,7 @@ __global__ void __launch_bounds__((TM / 4) * (EW / 4)) router_simt_logits_kernel
 // probabilities into the insertion top-k, reciprocal of the sum of the k selected.
 template <int KMAX>
 __device__ __forceinline__ void route_row(const float* __restrict__ l, int E, int k, float (&tv)[KMAX],
-                                          int (&ti)[KMAX], float& invs) {
+                                          int (&ti)[KMAX], float& invs, float* __restrict__ probs) {
   float m = -INFINITY;
   for (int e = 0; e < E; ++e) m = fmaxf(m, l[e]);
   float sum = 0.0f;
@@ -673,7 +678,11 @@ __device__ __forceinline__ void route_row(const float* __restrict__ l, int E, in
   const float inv = __frcp_rn(sum);
 #pragma unroll
   for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
-  for (int e = 0; e < E; ++e) topk_insert<KMAX>(tv, ti, __fmul_rn(softmax_exp(__fsub_rn(l[e], m)), inv), e);
+  for (int e = 0; e < E; ++e) {
+    const float p = __fmul_rn(softmax_exp(__fsub_rn(l[e], m)), inv);
+    if (probs) probs[e] = p;
+    topk_insert<KMAX>(tv, ti, p, e);
+  }
   float ssum = 0.0f;
 #pragma unroll
   for (int j = 0; j < KMAX; ++j)
@@ -692,7 +701,7 @@ __global__ void __launch_bounds__(kSmallTokens) router_small_route_kernel(const 
   if (t < T) {
     float tv[KMAX], invs;
     int ti[KMAX];
-    route_row<KMAX>(logits + (int64_t)t * E, E, k, tv, ti, invs);
+    route_row<KMAX>(logits + (int64_t)t * E, E, k, tv, ti, invs, a.probs ? a.probs + (int64_t)t * E : nullptr);
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
       if (j < k) {
@@ -754,7 +763,7 @@ __global__ void __launch_bounds__(kBM) router_route_logits_kernel(const float* _
   if (t < a.T) {
     float tv[KMAX], invs;
     int ti[KMAX];
-    route_row<KMAX>(logits + t * a.E, a.E, a.k, tv, ti, invs);
+    route_row<KMAX>(logits + t * a.E, a.E, a.k, tv, ti, invs, a.probs ? a.probs + t * a.E : nullptr);
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
       if (j < a.k) {
@@ -983,8 +992,8 @@ extern "C" int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const
                                           const float* gate_bias, int64_t num_tokens, int hidden_size,
                                           int num_experts, int top_k, int32_t* ids, float* weights,
                                           void* weights_bf16, int32_t* counts, int32_t* offsets, int32_t* sorted_idx,
-                                          int32_t* positions, float* logits, void* workspace, size_t workspace_bytes,
-                                          lmoe_stream_t stream_) {
+                                          int32_t* positions, float* logits, float* probs, void* workspace,
+                                          size_t workspace_bytes, lmoe_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   LMOE_ARG_CHECK(dtype_ok(x_dtype) && dtype_ok(w_dtype));
   LMOE_ARG_CHECK(num_tokens >= 0 && num_tokens <= (int64_t)INT32_MAX / 16);
@@ -1025,6 +1034,7 @@ extern "C" int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const
     a.offsets = offsets;
     a.sorted_idx = sorted_idx;
     a.positions = do_perm ? positions : nullptr;
+    a.probs = probs;
     a.do_perm = do_perm ? 1 : 0;
     a.err = reinterpret_cast<uint32_t*>(ws);
     a.T = (int)num_tokens;
@@ -1081,6 +1091,7 @@ extern "C" int lmoe_fused_gate_topk_typed(const void* hidden, int x_dtype, const
   a.weights = weights;
   a.weights_bf16 = static_cast<__nv_bfloat16*>(weights_bf16);
   a.logits = logits;
+  a.probs = probs;
   a.counts = counts;
   a.offsets = offsets;
   a.sorted_idx = sorted_idx;
@@ -1128,7 +1139,7 @@ extern "C" int lmoe_fused_gate_topk(const void* hidden, const void* gate_weight,
                                     void* workspace, size_t workspace_bytes, lmoe_stream_t stream) {
   return lmoe_fused_gate_topk_typed(hidden, LMOE_DTYPE_BF16, gate_weight, LMOE_DTYPE_BF16, gate_bias, num_tokens,
                                     hidden_size, num_experts, top_k, ids, weights, weights_bf16, counts, offsets,
-                                    sorted_idx, positions, logits, workspace, workspace_bytes, stream);
+                                    sorted_idx, positions, logits, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int lmoe_fused_gate_topk_static(const void* hidden, const void* gate_weight, const float* gate_bias,

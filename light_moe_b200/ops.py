@@ -47,10 +47,11 @@ def fused_gate_topk_permute(hidden_states, gate_weight, top_k):
     return extension().fused_gate_topk_permute(hidden_states, gate_weight, top_k)
 
 
-def fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias=None, return_logits=False):
+def fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias=None, return_logits=False, return_probs=False):
     """[ids int32, weights fp32, counts int32, offsets int32, sorted_idx int32, positions int32
-    (, logits fp32)] -- positions is the inverse permutation of sorted_idx."""
-    return extension().fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias, return_logits)
+    (, logits fp32 [T, E]) (, probs fp32 [T, E])] -- positions is the inverse permutation of
+    sorted_idx, probs the full softmax probabilities."""
+    return extension().fused_gate_topk_ex(hidden_states, gate_weight, top_k, bias, return_logits, return_probs)
 
 
 def quantize_w4(w, group_size):

@@ -26,6 +26,7 @@ from .core import (  # noqa: F401
     f16_bits_to_f32,
     ref_expf,
     route,
+    softmax_probs,
     counts_offsets,
     quantize_w4,
     dequantize_w4,

@@ -40,6 +40,8 @@ def load():
             lib = ctypes.CDLL(_LIB_PATH)
             lib.lmoe_ref_route.argtypes = [_P, _I32, _I32, _I32, _P, _P]
             lib.lmoe_ref_route.restype = _I32
+            lib.lmoe_ref_softmax.argtypes = [_P, _I32, _I32, _P]
+            lib.lmoe_ref_softmax.restype = _I32
             lib.lmoe_ref_counts_offsets.argtypes = [_P, _I32, _I32, _I32, _P, _P, _P]
             lib.lmoe_ref_counts_offsets.restype = _I32
             lib.lmoe_ref_quantize_w4.argtypes = [_P, _I64, _I32, _I32, _P, _P]
@@ -90,6 +92,17 @@ def ref_expf(x) -> np.ndarray:
     x = _c(x, np.float32)
     out = np.empty(x.shape, np.float32)
     load().lmoe_ref_expf_array(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def softmax_probs(logits) -> np.ndarray:
+    """The full fp32 softmax probabilities [T, E] with the routing's own arithmetic
+    (router_probs of python/light_moe/ops/moe_gate.py:66-67)."""
+    lg = _c(logits, np.float32)
+    T, E = lg.shape
+    out = np.empty((T, E), np.float32)
+    if load().lmoe_ref_softmax(_ptr(lg), T, E, _ptr(out)) != 0:
+        raise ValueError("oracle softmax: bad arguments")
     return out
 
 

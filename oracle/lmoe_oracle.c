@@ -181,6 +181,29 @@ int lmoe_ref_route(const float* logits, int T, int E, int k, int32_t* ids, float
 }
 
 /*
+ * The full softmax probabilities of the routing above (router_probs of
+ * python/light_moe/ops/moe_gate.py:20-36, computed by top_k_routing at :66-67): the same
+ * max, exponentials, sequential sum and reciprocal-multiply as lmoe_ref_route.
+ */
+int lmoe_ref_softmax(const float* logits, int T, int E, float* probs) {
+    if (T < 0 || E <= 0) return -1;
+    for (int t = 0; t < T; ++t) {
+        const float* l = logits + (size_t)t * E;
+        float* p = probs + (size_t)t * E;
+        float m = l[0];
+        for (int e = 1; e < E; ++e) m = fmaxf(m, l[e]);
+        float sum = 0.0f;
+        for (int e = 0; e < E; ++e) {
+            p[e] = lmoe_ref_expf(l[e] - m);
+            sum = sum + p[e];
+        }
+        float inv = 1.0f / sum;
+        for (int e = 0; e < E; ++e) p[e] = p[e] * inv;
+    }
+    return 0;
+}
+
+/*
  * Histogram, exclusive scan and stable permutation of the flattened assignment list.
  * ids: [T, k].  counts: [E], offsets: [E+1], sorted_idx: [T*k] with
  * sorted_idx[offsets[e] + r] = the r-th flat index t*k+j (in increasing order) whose

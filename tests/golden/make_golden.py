@@ -8,8 +8,9 @@ The reference cannot travel to the GPU machines, so its outputs are recorded her
 ``.npz`` fixtures (inputs + outputs) that ``tests/test_oracle.py`` replays against the CPU
 oracle.  What each fixture pins:
 
-* ``routing_*.npz``   -- ``light_moe.ops.moe_gate.top_k_routing`` (moe_gate.py:39-77) and the
-  ``MoEGate.forward`` counts (moe_gate.py:202-214) on fp32 logits without exact ties.
+* ``routing_*.npz``   -- ``light_moe.ops.moe_gate.top_k_routing`` (moe_gate.py:39-77), the
+  ``MoEGate.forward`` counts (moe_gate.py:202-214) and ``load_balancing_loss``
+  (moe_gate.py:80-122) on fp32 logits without exact ties.
 * ``permute_*.npz``   -- ``light_moe.ops.grouped_gemm.permute_tokens`` / ``unpermute_tokens``
   (grouped_gemm.py:202-279): offsets, and per-expert segment contents (the reference sort is
   unstable, so segments are compared as sorted lists).
@@ -83,11 +84,14 @@ def main():
         counts = torch.zeros(E, dtype=torch.int64)
         for j in range(k):
             counts += torch.bincount(idx[:, :, j].flatten(), minlength=E)
+        # the load-balancing loss of these routings (moe_gate.py:80-122)
+        aux = mg.load_balancing_loss(probs, idx, E)
         np.savez_compressed(os.path.join(HERE, f"routing_T{T}_E{E}_k{k}.npz"),
                             logits=logits, ids=idx.view(T, k).numpy().astype(np.int32),
                             weights=w.view(T, k).numpy().astype(np.float32),
                             probs=probs.view(T, E).numpy().astype(np.float32),
-                            counts=counts.numpy().astype(np.int64))
+                            counts=counts.numpy().astype(np.int64),
+                            aux_loss=np.float32(aux.item()))
         out[f"routing_{T}_{E}_{k}"] = True
 
     # ---- permute / unpermute ----

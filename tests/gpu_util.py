@@ -17,7 +17,7 @@ def read_error(ws: torch.Tensor) -> int:
     return int(out[0])
 
 
-def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
+def router(x, w, k, bias=None, perm=True, logits=True, positions=False, probs=False):
     """lmoe_fused_gate_topk_typed through the C ABI (x and w of any of bf16 / fp16 / fp32);
     returns numpy arrays."""
     T, d = x.shape
@@ -32,12 +32,13 @@ def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
     sidx = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if perm else None
     lg = torch.empty(T, E, dtype=torch.float32, device=dev) if logits else None
     pos = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev) if positions else None
+    pr = torch.empty(T, E, dtype=torch.float32, device=dev) if probs else None
     nbytes = capi.lib().lmoe_router_workspace_bytes_typed(T, E, xdt, wdt)
     ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
     capi.call("lmoe_fused_gate_topk_typed", x.data_ptr(), xdt, w.data_ptr(), wdt, capi.ptr(bias), T, d, E, k,
               ids.data_ptr(),
               wts.data_ptr(), wbf.data_ptr(), capi.ptr(counts), capi.ptr(offsets), capi.ptr(sidx), capi.ptr(pos),
-              capi.ptr(lg),
+              capi.ptr(lg), capi.ptr(pr),
               ws.data_ptr(), ws.numel(), stream())
     torch.cuda.synchronize()
     err = read_error(ws)
@@ -49,6 +50,8 @@ def router(x, w, k, bias=None, perm=True, logits=True, positions=False):
         out["logits"] = lg.cpu().numpy()
     if positions:
         out["positions"] = pos[: T * k].cpu().numpy()
+    if probs:
+        out["probs"] = pr.cpu().numpy()
     return out
 
 
