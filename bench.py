@@ -25,6 +25,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 D, FFN, E, TOPK, GROUP = 4096, 14336, 8, 2, 128
+METRIC = "W4A16 MoE-layer tokens/s (Mixtral-8x7B experts, prefill 8192 tokens/GPU)"
 T_PREFILL, T_DECODE = 8192, 64
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -125,6 +126,16 @@ def make_problem(T, device, seed=0):
     gx = torch.Generator(device=device).manual_seed(seed + 1)
     x = torch.randn(T, D, generator=gx, device=device).to(torch.bfloat16)
     return x, gw, ex
+
+
+def l2_note(ex, ws, T):
+    """How the timed steps relate to the 126 MB L2, per rank."""
+    w = (ex.w13_packed.numel() + ex.w2_packed.numel()) / ws / 1e6
+    act = T * TOPK * (D + FFN) * 2 / 1e6   # dispatched rows and the SwiGLU output, bf16
+    if w > 126:
+        return f"inputs larger than L2: {w:.0f} MB of int4 weights per GPU streamed every step"
+    return (f"{w:.0f} MB of int4 weights per GPU fit in the 126 MB L2, but every step also streams "
+            f"~{act:.0f} MB of dispatched rows and SwiGLU output per GPU, which evicts them")
 
 
 # ----------------------------------------------------------------------------- timing helpers
@@ -284,12 +295,67 @@ def extra_workloads(ex, stream, peaks, peak_kind, device):
     return out
 
 
-# ----------------------------------------------------------------------------- CPU oracle baseline
-def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
-    """The oracle's numpy restatement of SparseMoEBlock on the dequantised weights."""
-    import numpy as np
+# ----------------------------------------------------------------------------- CPU reference path
+def host_threads():
+    """(logical cores of the host, threads torch uses for CPU math)."""
+    import torch
+    return os.cpu_count(), torch.get_num_threads()
+
+
+def reference_block():
+    """The reference's own SparseMoEBlock (python/light_moe/model/moe_block.py:63-169) at the
+    layer's shapes, fp32 on the host, when its bytecode is staged under oracle/_ref
+    (oracle/stage_reference.py); else None."""
     import torch
 
+    from oracle.stage_reference import available, import_sparse_moe_block
+    if not available():
+        return None
+    SparseMoEBlock = import_sparse_moe_block()
+    torch.manual_seed(0)
+    blk = SparseMoEBlock(D, FFN, num_experts=E, top_k=TOPK).eval()
+    # N(0, 0.02) weights like the GPU workload (the values do not change the CPU work; the
+    # dequantised int4 values are N(0, 0.02) samples rounded to the int4 grid)
+    with torch.no_grad():
+        for prm in blk.parameters():
+            prm.normal_(0.0, 0.02)
+    return blk
+
+
+def time_reference_block(blk, tokens, steps, warmup, budget_s):
+    """Seconds per forward of ``blk`` on ``tokens`` tokens (torch fp32, all host threads).
+    Returns (seconds per step, steps timed): after one warm-up forward, fewer than ``steps``
+    are timed when ``steps`` of them would exceed ``budget_s``."""
+    import torch
+    x = torch.randn(1, tokens, D, generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        blk(x)
+        first = time.perf_counter() - t0
+        for _ in range(max(0, warmup - 1) if first * warmup < budget_s / 4 else 0):
+            blk(x)
+        n = max(1, min(steps, int(budget_s // max(first, 1e-6))))
+        t0 = time.perf_counter()
+        for _ in range(n):
+            blk(x)
+        el = time.perf_counter() - t0
+    return el / n, n
+
+
+def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
+    """The reference's own SparseMoEBlock on the host cores (oracle restatement if it is not
+    staged), on a bounded sample of the workload."""
+    import numpy as np
+
+    cores, threads = host_threads()
+    blk = reference_block()
+    if blk is not None:
+        secs, n = time_reference_block(blk, tokens, 1000, 1, seconds_budget)
+        del blk
+        return {"value": round(tokens / secs, 2), "unit": "tokens/s", "cores": threads, "host_cores": cores,
+                "kind": "reference",
+                "sample": f"{n} forward(s) of light_moe SparseMoEBlock (fp32, torch, {threads} threads) on "
+                          f"{tokens} tokens of the layer"}
     import oracle
     from light_moe_b200 import ops
 
@@ -298,11 +364,9 @@ def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
     w3 = ops.dequantize_w4(c["q3"], c["s3"], GROUP).float().cpu().numpy()
     w2 = ops.dequantize_w4(c["q2"], c["s2"], GROUP).float().cpu().numpy()
     gwn = gw.float().cpu().numpy()
-    rng = np.random.default_rng(1)
-    x = rng.standard_normal((tokens, D), dtype=np.float32)
+    x = np.random.default_rng(1).standard_normal((tokens, D), dtype=np.float32)
     oracle.moe_layer_ref(x[:8], gwn, w1, w3, w2, TOPK)  # warm-up
-    done, t0 = 0, time.perf_counter()
-    reps = 0
+    done, reps, t0 = 0, 0, time.perf_counter()
     while True:
         oracle.moe_layer_ref(x, gwn, w1, w3, w2, TOPK)
         done += tokens
@@ -310,12 +374,8 @@ def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
         el = time.perf_counter() - t0
         if el > seconds_budget or reps >= 3:
             break
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        threads = os.cpu_count()
-    return done / el, threads, f"{reps} x {tokens} tokens through the fp32 numpy SparseMoEBlock restatement"
+    return {"value": round(done / el, 2), "unit": "tokens/s", "cores": threads, "host_cores": cores, "kind": "port",
+            "sample": f"{reps} x {tokens} tokens through the fp32 numpy SparseMoEBlock restatement"}
 
 
 # ----------------------------------------------------------------------------- arms
@@ -382,9 +442,39 @@ def run_ours(args):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = T * ws * args.steps / te.item()
 
+    ep_check = None
+    roof_ep = None
+    if ws > 1:
+        # parity of the expert-parallel step on every rank: its output against the
+        # single-GPU layer (all experts on this GPU) on the rank's own tokens
+        y_ep = fwd(x)
+        y_one = W4A16MoELayer(gw, ex, TOPK)(x)
+        rel = ((y_ep.float() - y_one.float()).abs().max() / y_one.float().abs().max()).double().reshape(1)
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
+        ep_check = float(rel.item())
+        # the per-rank gate/up GEMM inside the expert-parallel step (events around the launch)
+        layer.backend.gemm_timer = []
+        for _ in range(3):
+            fwd(x)
+        torch.cuda.synchronize()
+        times = [(a.elapsed_time(b) / 1e3, rows) for a, b, rows in layer.backend.gemm_timer]
+        layer.backend.gemm_timer = None
+        g_secs = sum(t for t, _ in times) / len(times)
+        g_rows = sum(r for _, r in times) / len(times)
+        tf = 2.0 * g_rows * (2 * FFN) * D / g_secs / 1e12
+        agg = torch.tensor([tf, -tf], device=device, dtype=torch.float64)
+        dist.all_reduce(agg, op=dist.ReduceOp.MAX)
+        roof_ep = {"kernel": "grouped_gemm_kernel<192,...,W4> gate/up+SwiGLU (this rank's experts, inside the EP step)",
+                   "bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                   "frac": round(tf / peaks["bf16_tflops"], 4), "peak_source": f"{peak_kind} bf16 burst",
+                   "launch_us": round(g_secs * 1e6, 1), "rows": round(g_rows, 1),
+                   "ranks_max_tflops": round(agg[0].item(), 1), "ranks_min_tflops": round(-agg[1].item(), 1),
+                   "algorithmic": {"flops": 2.0 * g_rows * (2 * FFN) * D}, "traffic": None,
+                   "traffic_unit": "DRAM bytes per launch (ncu); not captured for the per-rank launch"}
+
     result = None
     if rank == 0:
-        roof = gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind)
+        roof = roof_ep if ws > 1 else gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind)
         # decode sub-measurement (64 tokens per GPU)
         xd = x[:T_DECODE].contiguous()
         if ws > 1:
@@ -410,10 +500,9 @@ def run_ours(args):
                 extra = {"error": f"{type(exc).__name__}: {exc}"}
         cpu = None
         if not args.no_cpu_baseline and ws == 1:   # the CPU baseline is a single-GPU (rank 0, N=1) figure
-            v, cores, sample = cpu_baseline(ex, gw, args.cpu_tokens)
-            cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+            cpu = cpu_baseline(ex, gw, args.cpu_tokens)
         result = {
-            "metric": "W4A16 MoE-layer tokens/s (Mixtral-8x7B experts, prefill 8192 tokens/GPU)",
+            "metric": METRIC,
             "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, int4 weights, fp32 accumulate",
@@ -422,13 +511,14 @@ def run_ours(args):
                        "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP,
                        "parallelism": f"ep{ws}" if ws > 1 else "single GPU",
                        "ep_micro_batches": args.micro_batches if ws > 1 else None,
-                       "l2": "inputs larger than L2 (727 MB int4 weights streamed every step)"},
+                       "l2": l2_note(ex, ws, T)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                     "d2h_bytes_per_step": T * D * 2,
                     "call": ("W4A16MoELayer.forward_host (pinned host buffers, copies of one token range "
                              "overlapped with the kernels of the next)" if ws == 1 else
                              "pinned host x -> device, ExpertParallelW4A16Layer.forward, y -> pinned host")},
             "gpu_launches": launches_per_step * args.steps,
+            "ep_max_rel_err": ep_check,
             "roofline": roof,
             "decode": decode,
             "other_workloads": extra,
@@ -443,42 +533,48 @@ def run_ours(args):
 
 
 def run_reference(args):
-    """CPU arm: the oracle's fp32 numpy restatement of light-moe's SparseMoEBlock."""
+    """CPU arm: light-moe's own SparseMoEBlock (staged bytecode of the reference package) in
+    fp32 torch on the host cores, on the headline workload (8192 tokens per step); the
+    oracle's numpy restatement when the reference is not staged."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return None
     import numpy as np
 
-    import oracle
-
-    tokens = args.cpu_tokens
-    rng = np.random.default_rng(0)
-    gw = (rng.standard_normal((E, D), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
-    # fp32 expert weights of the layer's shapes (the CPU path runs on dequantised int4 values;
-    # the values do not change its work, so they are drawn directly)
-    w = {name: (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
-         for name, shape in (("w1", (E, FFN, D)), ("w3", (E, FFN, D)), ("w2", (E, D, FFN)))}
-    x = rng.standard_normal((tokens, D), dtype=np.float32)
-    for _ in range(args.warmup):
+    cores, threads = host_threads()
+    tokens = args.tokens
+    blk = reference_block()
+    budget = 180.0
+    if blk is not None:
+        secs, n = time_reference_block(blk, tokens, args.steps, args.warmup, budget)
+        kind = "reference"
+        sample = (f"light_moe SparseMoEBlock.forward (python/light_moe/model/moe_block.py:119-169), fp32 torch, "
+                  f"{threads} threads, {tokens} tokens per step, {n} timed step(s)")
+    else:
+        import oracle
+        rng = np.random.default_rng(0)
+        gw = (rng.standard_normal((E, D), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        w = {name: (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+             for name, shape in (("w1", (E, FFN, D)), ("w3", (E, FFN, D)), ("w2", (E, D, FFN)))}
+        x = rng.standard_normal((tokens, D), dtype=np.float32)
+        t0 = time.perf_counter()
         oracle.moe_layer_ref(x, gw, w["w1"], w["w3"], w["w2"], TOPK)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.moe_layer_ref(x, gw, w["w1"], w["w3"], w["w2"], TOPK)
-    el = time.perf_counter() - t0
-    value = tokens * args.steps / el
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count()
-    res = {"impl": "reference", "metric": "W4A16 MoE-layer tokens/s (Mixtral-8x7B experts, prefill 8192 tokens/GPU)",
-           "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "fp32 (dequantised int4 weights)", "data": "synthetic",
-           "config": {"workload": "Mixtral-8x7B-shaped W4A16 MoE layer, prefill", "tokens_per_step": tokens,
+        first = time.perf_counter() - t0
+        n = max(1, min(args.steps, int(budget // max(first, 1e-6))))
+        t0 = time.perf_counter()
+        for _ in range(n):
+            oracle.moe_layer_ref(x, gw, w["w1"], w["w3"], w["w2"], TOPK)
+        secs = (time.perf_counter() - t0) / n
+        kind = "port"
+        sample = f"oracle numpy restatement of SparseMoEBlock, {tokens} tokens per step, {n} timed step(s)"
+    value = tokens / secs
+    res = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
+           "steps": n, "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (host)", "data": "synthetic (seeded)",
+           "config": {"workload": "Mixtral-8x7B-shaped MoE layer, prefill", "tokens_per_step": tokens,
                       "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP},
-           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": f"{tokens} tokens per step (bounded sample of the 8192-token batch)"},
+           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "host_cores": cores,
+                            "kind": kind, "sample": sample},
            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
     return res
@@ -491,7 +587,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
-    ap.add_argument("--cpu-tokens", type=int, default=512)
+    ap.add_argument("--cpu-tokens", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the router / skewed-GEMM / fine-grained measurements")
     ap.add_argument("--micro-batches", type=int, default=1,

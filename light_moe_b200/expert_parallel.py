@@ -125,6 +125,9 @@ class CudaExpertBackend:
         self.top_k = top_k
         self.num_local = local.num_experts      # routed experts on this rank
         self.num_shared = local.num_shared
+        # when a list, every gate/up GEMM appends (start event, end event, rows) on the current
+        # stream (used to time the per-rank kernel inside an expert-parallel step)
+        self.gemm_timer = None
 
     def route(self, x, gate_weight, gate_bias):
         ids, w, counts, offsets, sidx, pos = ops.fused_gate_topk_ex(x, gate_weight, self.top_k, gate_bias)[:6]
@@ -140,8 +143,15 @@ class CudaExpertBackend:
 
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         e = self.ex
+        if self.gemm_timer is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
         h = ops.w4a16_grouped_gemm(rows, e.w13_packed, seg_offsets, num_seg, 2 * e.ffn_size, e.group_size, 1,
                                    None, None, 0, max_rows, seg_expert)
+        if self.gemm_timer is not None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            self.gemm_timer.append((ev0, ev1, rows.shape[0]))
         return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
                                       None, None, 0, max_rows, seg_expert)
 

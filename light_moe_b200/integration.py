@@ -100,7 +100,8 @@ class SparseMoEBlockW4A16(torch.nn.Module):
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         experts = W4A16Experts.from_dense(wts["w1"].to(dev), wts["w3"].to(dev), wts["w2"].to(dev), group_size)
         gb = wts["gate_bias"].to(dev) if wts["gate_bias"] is not None else None
-        return cls(wts["gate"].to(dev), experts, wts["top_k"], gate_bias=gb, aux_loss_coef=wts["aux_loss_coef"])
+        mod = cls(wts["gate"].to(dev), experts, wts["top_k"], gate_bias=gb, aux_loss_coef=wts["aux_loss_coef"])
+        return mod.train(getattr(block, "training", False))
 
     def forward(self, hidden_states: torch.Tensor):
         shape = hidden_states.shape

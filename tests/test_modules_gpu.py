@@ -81,7 +81,8 @@ def test_block_conversion(layout):
         for p in blk.parameters():
             p.mul_(0.05 if p.dim() == 3 else 1.0)
     blk = blk.to(torch.bfloat16)
-    mod = integration.SparseMoEBlockW4A16.from_block(blk, group_size=128)
+    mod = integration.SparseMoEBlockW4A16.from_block(blk.eval(), group_size=128)
+    assert not mod.training
     x = torch.randn(3, 40, d, device="cuda").to(torch.bfloat16)
     y, aux = mod(x)
     assert y.shape == x.shape and y.dtype == x.dtype and aux is None
