@@ -39,8 +39,9 @@
 // SwiGLU, 256 B otherwise) with 16-byte stores; for SwiGLU the gate lanes (0-63) and up lanes
 // (64-127) exchange half of the step's columns so all four epilogue warps compute.
 //
-// Tile order: segment-major, then feature block, then token block (fastest), so the CTAs
-// working at the same time share each weight block through L2.
+// Tile order: segment-major; inside a segment the larger operand is the slow index (feature
+// blocks for the gate/up projection, token blocks for the down projection of a prefill
+// batch), so the CTAs working at the same time share its tiles through L2.
 //
 // Epilogue modes:
 //   kPlain   out[r, n]                                        = bf16(acc)
@@ -82,6 +83,7 @@ struct GemmArgs {
   int ab_f16;                 // dense operands fp16 (else bf16); plain outputs written as fp16
   int num_w;                  // weight matrices available
   int64_t R;                  // activation rows
+  int raster_rows;            // segments with more rows run token-block-major (tile_at)
 };
 
 // fp32 -> the 16-bit output type (bf16, or fp16 for fp16 operands), as bf16 storage.
@@ -146,9 +148,14 @@ struct TileInfo {
   int e, w, fb, row0, rows;   // segment, its weight matrix, feature block, first row, rows
 };
 
-// Tiles are numbered segment-major, then feature block, then token block (fastest).
+// Tiles are numbered segment-major; inside a segment, feature block then token block
+// (fastest) when the segment's weight matrix is the larger operand, token block then
+// feature block (fastest) when its activation rows are: the CTAs working at the same time
+// then share the larger operand through L2 and each tile of it is read from HBM about once.
+// (Activations rows x K x 2 bytes against weights N x K x 2 bytes, or N x K / 2 for int4:
+// token blocks first when rows > raster_rows = N, or N / 4.)
 template <int BN>
-__device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_hint) {
+__device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_hint, int NB, int raster_rows) {
   int e = e_hint;
   while (tile >= b->tile_start[e + 1]) ++e;
   e_hint = e;
@@ -158,8 +165,14 @@ __device__ __forceinline__ TileInfo tile_at(const GemmBars* b, int tile, int& e_
   TileInfo ti;
   ti.e = e;
   ti.w = b->seg_w[e];
-  ti.fb = local / ntb;
-  const int tb = local - ti.fb * ntb;
+  int tb;
+  if (n_e > raster_rows) {
+    tb = local / NB;
+    ti.fb = local - tb * NB;
+  } else {
+    ti.fb = local / ntb;
+    tb = local - ti.fb * ntb;
+  }
   ti.row0 = b->row_off[e] + tb * BN;
   const int left = n_e - tb * BN;
   ti.rows = left < BN ? left : BN;
@@ -228,9 +241,12 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
     bars->tile_start[0] = 0;
     for (int e = 0; e < a.E; ++e) {
       int n_e = bars->row_off[e + 1] - bars->row_off[e];
-      // a segment whose rows or weight matrix lie outside the buffers is skipped
-      if (n_e < 0 || bars->row_off[e] < 0 || bars->row_off[e + 1] > a.R || bars->seg_w[e] < 0 ||
-          bars->seg_w[e] >= a.num_w) {
+      // a hole (weight matrix -1, rows in range) is skipped silently; a segment whose rows
+      // or weight matrix lie outside the buffers is skipped and reported
+      const bool rows_ok = n_e >= 0 && bars->row_off[e] >= 0 && bars->row_off[e + 1] <= a.R;
+      if (rows_ok && bars->seg_w[e] == -1) {
+        n_e = 0;
+      } else if (!rows_ok || bars->seg_w[e] < 0 || bars->seg_w[e] >= a.num_w) {
         if (n_e != 0) report_error(a.err, kErrBadArg, kSite + 9);
         n_e = 0;
       }
@@ -257,10 +273,10 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
       uint32_t it = 0, it_w = 0;
       int e_hint = 0, w_hint = 0, tile_w = blockIdx.x, ks_w = 0;
       TileInfo ti_w = {};
-      if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint);
+      if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint, a.NB, a.raster_rows);
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
+        const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB, a.raster_rows);
         const int nbox = (ti.rows + BOX - 1) / BOX;   // only the boxes that cover this tile's rows
         const uint32_t bytes = (uint32_t)(2 * nbox * BOX * kBK * 2);
         for (int ks = 0; ks < KS; ++ks, ++it) {
@@ -289,7 +305,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
             if (++ks_w == KS) {
               ks_w = 0;
               tile_w += gridDim.x;
-              if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint);
+              if (tile_w < total) ti_w = tile_at<BN>(bars, tile_w, w_hint, a.NB, a.raster_rows);
             }
           }
           if (!ok) break;
@@ -323,7 +339,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
       int e_hint = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++lt) {
-        const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
+        const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB, a.raster_rows);
         const int n_eff = (ti.rows + 15) & ~15;
         int n_mine = n_eff - half * (BN / 2);   // this issuer's columns, a multiple of 16
         n_mine = n_mine < 0 ? 0 : (n_mine > BN / 2 ? BN / 2 : n_mine);
@@ -475,7 +491,7 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
     uint32_t lt = 0, chunk = 0;
     int e_hint = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++lt) {
-      const TileInfo ti = tile_at<BN>(bars, tile, e_hint);
+      const TileInfo ti = tile_at<BN>(bars, tile, e_hint, a.NB, a.raster_rows);
       const int n_eff = (ti.rows + 15) & ~15;
       const uint32_t acc = lt % ACC;
       if (!mbar_wait(&bars->acc_full[acc], (lt / ACC) & 1u, a.err, abort_flag, kSite + 12)) break;
@@ -670,6 +686,7 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.ab_f16 = (!w4 && p.ab_f16) ? 1 : 0;
   a.num_w = p.num_w > 0 ? p.num_w : p.num_experts;
   a.R = p.total_rows;
+  a.raster_rows = w4 ? p.N / 4 : p.N;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
   // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),

@@ -125,6 +125,28 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_INVALID_ARG;
 }
 
+int encode_tmap_kblocks(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                        uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows,
+                        uint32_t box_blocks) {
+  // the driver entry point is resolved by encode_tmap_2d's first call
+  if (!g_encode) {
+    CUtensorMap tmp;
+    encode_tmap_2d(&tmp, base, dtype, elem_bytes, 1, 128 / elem_bytes, row_stride_bytes, 1, 128 / elem_bytes, true);
+  }
+  if (!g_encode) return LMOE_ERR_DEVICE;
+  const uint64_t blk = 128 / elem_bytes;   // elements per 128-byte block
+  if (!aligned16(base) || (row_stride_bytes % 16) != 0 || cols % blk != 0) return LMOE_ERR_INVALID_ARG;
+  if (box_rows == 0 || box_rows > 256 || box_blocks == 0 || box_blocks > 256) return LMOE_ERR_INVALID_ARG;
+  cuuint64_t gdim[3] = {blk, rows, cols / blk};
+  cuuint64_t gstride[2] = {row_stride_bytes, 128};
+  cuuint32_t box[3] = {(cuuint32_t)blk, box_rows, box_blocks};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_INVALID_ARG;
+}
+
 }  // namespace lmoe
 
 extern "C" int lmoe_version(void) { return 100; }

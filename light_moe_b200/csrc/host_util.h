@@ -53,6 +53,14 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
                    uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols,
                    bool swizzle128);
 
+// Encode a row-major `rows` x `cols` matrix (row pitch `row_stride_bytes`) as a 3-D tensor
+// of 128-byte column blocks: dims {block elements, rows, cols / block elements}, so one box
+// {block elements, box_rows, box_blocks} lands in shared memory as [box_blocks][box_rows]
+// [128 bytes] with the 128-byte swizzle -- several K blocks of a row tile in one copy.
+int encode_tmap_kblocks(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                        uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows,
+                        uint32_t box_blocks);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace lmoe

@@ -76,6 +76,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test: has the phase with the given parity completed?  (try_wait may
+// suspend the thread for a while; a thread that serves several queues polls with this.)
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  On timeout the error
 // word receives kErrTimeout|site, *abort is raised for the rest of the CTA, and false is
 // returned.  A raised *abort makes every later wait give up immediately.
@@ -129,6 +143,45 @@ __device__ __forceinline__ bool counter_wait(const uint32_t* ctr, uint32_t targe
   }
 }
 
+// Four counters (16-byte aligned, one per writing warp) read with one relaxed vector load;
+// returns the smallest.
+__device__ __forceinline__ uint32_t min4_relaxed_shared(const uint32_t* p) {
+  uint32_t a, b, c, d;
+  asm volatile("ld.relaxed.cta.shared::cta.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(smem_u32(p))
+               : "memory");
+  return min(min(a, b), min(c, d));
+}
+__device__ __forceinline__ void fence_acq_rel_cta() { asm volatile("fence.acq_rel.cta;" ::: "memory"); }
+
+// Bounded wait until all four counters at p exceed target (acquire: relaxed polls, then one
+// fence once they do).  *seen receives the smallest value read.  Same error / abort
+// contract as mbar_wait.
+__device__ __forceinline__ bool counter4_wait(const uint32_t* p, uint32_t target, uint32_t* seen, uint32_t* err,
+                                              volatile int* abort, uint32_t site) {
+  uint32_t m = min4_relaxed_shared(p);
+  if (m <= target) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (true) {
+      m = min4_relaxed_shared(p);
+      if (m > target) break;
+      if (((++spins) & 255u) == 0u) {
+        if (abort && *abort) return false;
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          report_error(err, kErrTimeout, site);
+          if (abort) *abort = 1;
+          return false;
+        }
+      }
+    }
+  }
+  fence_acq_rel_cta();
+  if (seen) *seen = m;
+  return true;
+}
+
 // ---------------------------------------------------------------------------------------
 // TMA
 // ---------------------------------------------------------------------------------------
@@ -143,6 +196,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 

@@ -18,20 +18,31 @@ namespace lmoe {
 __device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __nv_bfloat162 bits_bf16x2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
 
-// Dequantise one 16-byte half-row (32 K values) into the 16 bf16x2 registers of its K pairs
-// in order: pair m = 4i + c lives in word c, slot i.
-__device__ __forceinline__ void dequant_half(const uint4 v, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo,
-                                             const __nv_bfloat162 off136, uint32_t (&o)[16]) {
+// One 16-byte half-row (w4_layout.cuh) -> the bf16x2 bits of (128 + u) for its 16 K pairs
+// in K order (o[m] = pair m: K 2m in the low half, 2m + 1 in the high half).
+__device__ __forceinline__ void w4_unpack_half(const uint4 v, uint32_t (&o)[16]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
+    const uint32_t lo = w[c] & 0x0F0F0F0Fu;           // pairs 4c, 4c+1
+    const uint32_t hi = (w[c] >> 4) & 0x0F0F0F0Fu;    // pairs 4c+2, 4c+3
+    o[4 * c + 0] = __byte_perm(lo, 0x43434343u, 0x5140);
+    o[4 * c + 1] = __byte_perm(lo, 0x43434343u, 0x7362);
+    o[4 * c + 2] = __byte_perm(hi, 0x43434343u, 0x5140);
+    o[4 * c + 3] = __byte_perm(hi, 0x43434343u, 0x7362);
+  }
+}
+
+// Dequantise one 16-byte half-row (32 K values) into the 16 bf16x2 registers of its K pairs
+// in K order.
+__device__ __forceinline__ void dequant_half(const uint4 v, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo,
+                                             const __nv_bfloat162 off136, uint32_t (&o)[16]) {
+  w4_unpack_half(v, o);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t x = ((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16 pair (128 + u)
-      const __nv_bfloat162 q = __hsub2(bits_bf16x2(x), off136);            // exact q = u - 8
-      const __nv_bfloat162 t = __hmul2(q, s_lo);                            // exact (<= 6 bits)
-      o[4 * i + c] = bf16x2_bits(__hfma2(q, s_hi, t));                      // one rounding of q*s
-    }
+  for (int m = 0; m < 16; ++m) {
+    const __nv_bfloat162 q = __hsub2(bits_bf16x2(o[m]), off136);   // exact q = u - 8
+    const __nv_bfloat162 t = __hmul2(q, s_lo);                      // exact (<= 6 bits)
+    o[m] = bf16x2_bits(__hfma2(q, s_hi, t));                        // one rounding of q*s
   }
 }
 

@@ -16,14 +16,16 @@
 //   super-block carries the scale of the group that contains it);
 //   packed [E][NB = rows/128][K/128][super-block]
 //
-//   inside each 16-byte half-row (32 consecutive K values, octets i = 0..3 of 8 values) the
-//   nibbles are transposed and interleaved: 32-bit word c (c = 0..3) holds, in slot i, the
-//   pair (k = 8i + 2c, 8i + 2c + 1):  bits [4i, 4i+4) = k 8i+2c,  bits [16+4i, 20+4i) = k 8i+2c+1.
-//   So (word >> 4i) & 0x000F000F places one K pair in the two bf16 halves, and
-//   * a thread that owns a whole row (tcgen05 path) gets every pair of its 32 K values from
-//     its 16 bytes (pair m = 4i + c comes from word c, slot i);
-//   * ldmatrix of 8 rows x 16 bytes gives mma.sync thread (g, c) word c of row g: exactly the
-//     A-fragment pairs (k 2c, 2c+1) of the half's four octets (two 16-wide k steps).
+//   inside each 16-byte half-row (32 consecutive K values = 16 pairs (2m, 2m+1), m = 0..15;
+//   lo(m) / hi(m) the nibbles of K 2m / 2m+1) the nibbles are regrouped so that one AND or
+//   one shift+AND exposes four pairs in four bytes: 32-bit word c (c = 0..3) holds pairs
+//   4c..4c+3 as
+//     byte 0 = lo(4c)   | lo(4c+2) << 4      byte 1 = hi(4c)   | hi(4c+2) << 4
+//     byte 2 = lo(4c+1) | lo(4c+3) << 4      byte 3 = hi(4c+1) | hi(4c+3) << 4
+//   so w & 0x0F0F0F0F = [lo(4c), hi(4c), lo(4c+1), hi(4c+1)] and (w >> 4) & 0x0F0F0F0F the
+//   same for pairs 4c+2, 4c+3, and one byte permute per pair builds the bf16 pair
+//   (128 + lo, 128 + hi) with the exponent byte 0x43 (w4_dequant.cuh).  A thread that owns a
+//   whole row reads its 16 bytes and gets the 16 pairs in K order.
 //
 // Gate/up ("paired") prepacking interleaves two matrices A (gate, w1) and B (up, w3) of
 // F rows each by 64-row blocks: block fb holds rows fb*64.. of A in rows 0..63 and the same
@@ -41,32 +43,20 @@ constexpr int kW4SuperInt4Bytes = 2 * kW4KBlockBytes;            // 8192
 __host__ __device__ constexpr int w4_scale_groups(int g) { return g >= kW4SuperK ? 1 : kW4SuperK / g; }
 __host__ __device__ constexpr int w4_super_bytes(int g) { return kW4SuperInt4Bytes + 256 * w4_scale_groups(g); }
 
-// Bytes b_i = (k_{2i} | k_{2i+1} << 4), i = 0..3 -> low nibbles in bits [4i, 4i+4), high
-// nibbles in bits [16+4i, 20+4i).
-__host__ __device__ __forceinline__ uint32_t w4_split_nibbles(uint32_t c) {
-  uint32_t lo = c & 0x0F0F0F0Fu;
-  uint32_t hi = (c >> 4) & 0x0F0F0F0Fu;
-  lo = (lo | (lo >> 4)) & 0x00FF00FFu;
-  hi = (hi | (hi >> 4)) & 0x00FF00FFu;
-  lo = (lo & 0xFFu) | ((lo >> 8) & 0xFF00u);
-  hi = (hi & 0xFFu) | ((hi >> 8) & 0xFF00u);
-  return lo | (hi << 16);
+// Canonical 16 bytes of a half-row (byte m = lo(m) | hi(m) << 4, m = 0..15) -> device words.
+// Word c is built from canonical word c alone (pairs 4c..4c+3).
+__host__ __device__ __forceinline__ uint32_t w4_device_word(uint32_t v) {
+  const uint32_t b0 = v & 0xFFu, b1 = (v >> 8) & 0xFFu, b2 = (v >> 16) & 0xFFu, b3 = v >> 24;
+  const uint32_t d0 = (b0 & 0x0Fu) | ((b2 & 0x0Fu) << 4);
+  const uint32_t d1 = (b0 >> 4) | (b2 & 0xF0u);
+  const uint32_t d2 = (b1 & 0x0Fu) | ((b3 & 0x0Fu) << 4);
+  const uint32_t d3 = (b1 >> 4) | (b3 & 0xF0u);
+  return d0 | (d1 << 8) | (d2 << 16) | (d3 << 24);
 }
 
-// Canonical 16 bytes of a half-row (byte b = k 2b | k 2b+1 << 4, b = 0..15) -> device words.
-// Word c gathers canonical byte 4i + c of every octet i (a 4 x 4 byte transpose) and splits
-// the nibbles.
 __host__ __device__ __forceinline__ uint4 w4_device_half(uint4 canon) {
-  const uint32_t w[4] = {canon.x, canon.y, canon.z, canon.w};
-  uint32_t t[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t v = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v |= ((w[i] >> (8 * c)) & 0xFFu) << (8 * i);
-    t[c] = w4_split_nibbles(v);
-  }
-  return make_uint4(t[0], t[1], t[2], t[3]);
+  return make_uint4(w4_device_word(canon.x), w4_device_word(canon.y), w4_device_word(canon.z),
+                    w4_device_word(canon.w));
 }
 
 }  // namespace lmoe
