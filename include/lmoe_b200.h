@@ -199,7 +199,9 @@ int lmoe_grouped_gemm_bf16(const void* input, int64_t total_rows, int K, const v
  *             output[r, f] = silu(gate[r, f]) * up[r, f]         (ldo >= F)
  * epilogue 2: output[dest_rows[r], n] = row_scale[r] * acc       (NULL = identity / 1)
  * segment_expert: weight matrix used by each of the num_experts row segments (NULL: the
- *             identity), so rows grouped by (source, expert) need no re-sort.
+ *             identity), so rows grouped by (source, expert) need no re-sort; -1 marks a
+ *             hole (padding rows of a fixed-capacity exchange): its rows are skipped and
+ *             their output rows are left untouched.
  * num_weight_matrices: matrices held by `packed`; every segment_expert entry (or, without a
  *             map, every segment index) must lie in [0, num_weight_matrices).  A kernel that
  *             finds an entry outside it, or offsets that decrease or pass total_rows, skips

@@ -28,6 +28,17 @@ enqueued back to back on NCCL's stream while the GEMMs of micro-batch m run on t
 stream, and the combine all-to-all of m overlaps the GEMMs of m + 1.  Each token's
 arithmetic is unchanged.
 
+With ``dispatch="capacity"`` (decode: small batches of at most ``capacity_tokens`` tokens
+per rank, the same bound on every rank) nothing is copied to the host: every rank sends
+every other rank a fixed block of C = capacity_tokens * top_k rows (its rows for that rank,
+then padding), so both all-to-alls have equal, host-known splits; the per-(rank, expert)
+counts still travel in a small all-to-all, but only the device reads them -- the segment
+offsets are prefix sums on the device, each source rank's padding is a "hole" segment
+(weight matrix -1, skipped by the GEMMs), and the combine reads the returned block through
+the padded positions of the rank's own sorted rows.  The whole step can be captured in a
+CUDA graph.  The reference pads to equal splits as well (expert_parallel.py:186-244) but
+sends every token to every rank; here only the routed rows carry data.
+
 The steps that move data between ranks use ``torch.distributed`` collectives, so the
 whole flow also runs with the gloo backend on CPU processes when a CPU expert backend is
 supplied (the tests do this); the product backend is the CUDA library.
@@ -163,8 +174,15 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
     """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks."""
 
     def __init__(self, config: ExpertParallelConfig, ep_group: ExpertParallelGroup, gate_weight: torch.Tensor,
-                 backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1):
+                 backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1,
+                 dispatch: str = "exact", capacity_tokens: Optional[int] = None):
         super().__init__()
+        if dispatch not in ("exact", "capacity"):
+            raise ValueError(f"dispatch must be 'exact' or 'capacity', not {dispatch!r}")
+        if dispatch == "capacity" and (capacity_tokens is None or int(capacity_tokens) < 1):
+            raise ValueError("capacity dispatch needs capacity_tokens >= 1 (the same on every rank)")
+        self.dispatch = dispatch
+        self.capacity_tokens = int(capacity_tokens) if capacity_tokens is not None else None
         self.config = config
         self.ep_group = ep_group
         self.gate_weight = gate_weight
@@ -182,7 +200,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
     @classmethod
     def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
                   group: Optional[dist.ProcessGroup] = None, gate_bias: Optional[torch.Tensor] = None,
-                  micro_batches: int = 1):
+                  micro_batches: int = 1, dispatch: str = "exact", capacity_tokens: Optional[int] = None):
         """Build this rank's layer from the full (all-expert) prepacked weights."""
         ws = dist.get_world_size(group)
         g = ExpertParallelGroup(ws).attach(group)
@@ -193,7 +211,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
                                    num_shared=experts.num_shared)
         local = slice_experts(experts, g.rank * cfg.experts_per_rank, (g.rank + 1) * cfg.experts_per_rank)
         return cls(cfg, g, gate_weight.to(torch.bfloat16).contiguous(), CudaExpertBackend(local, top_k), gate_bias,
-                   micro_batches)
+                   micro_batches, dispatch, capacity_tokens)
 
     def _segments(self, device):
         key = (str(device),)
@@ -203,8 +221,68 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             self._seg_cache[key] = torch.tensor(seg, dtype=torch.int32, device=device)
         return self._seg_cache[key]
 
+    def _capacity_segments(self, device):
+        key = ("cap", str(device))
+        if key not in self._seg_cache:
+            ep, epr, S = self.ep_group.ep_size, self.experts_per_rank, self.config.num_shared
+            seg = [e if e < epr else -1 for _ in range(ep) for e in range(epr + 1)] + [epr + s for s in range(S)]
+            self._seg_cache[key] = torch.tensor(seg, dtype=torch.int32, device=device)
+        return self._seg_cache[key]
+
+    def _forward_capacity(self, x: torch.Tensor) -> torch.Tensor:
+        T, d = x.shape
+        cfg, g, be = self.config, self.ep_group, self.backend
+        ep, epr, k, S = g.ep_size, self.experts_per_rank, cfg.top_k, cfg.num_shared
+        if T > self.capacity_tokens:
+            raise ValueError(f"{T} tokens exceed capacity_tokens={self.capacity_tokens}")
+        C = self.capacity_tokens * k                  # rows per destination block
+        dev = x.device
+        self.kernels_per_step = 5
+        if T > 0:
+            ids, w, counts, offsets, sidx, pos = be.route(x, self.gate_weight, self.gate_bias)
+            counts = counts.view(ep, epr).to(torch.int32)
+            # sorted row j (destination-rank order) -> padded send row r(j) * C + j - start[r(j)]
+            cnt_r = counts.sum(1)
+            end_r = torch.cumsum(cnt_r, 0)
+            start_r = end_r - cnt_r
+            j = torch.arange(T * k, device=dev, dtype=end_r.dtype)
+            r_of_j = torch.searchsorted(end_r, j, right=True)
+            p = r_of_j * C + (j - start_r[r_of_j])
+            # padded send block: slot r * C + c holds sorted row start[r] + c (padding: row 0)
+            c = torch.arange(C, device=dev, dtype=end_r.dtype)
+            src = (start_r[:, None] + c[None, :]).clamp(max=T * k - 1)
+            padded_sidx = torch.where(c[None, :] < cnt_r[:, None], sidx.long()[src], torch.zeros_like(src))
+            send = be.gather(x, padded_sidx.to(torch.int32).flatten())
+        else:
+            counts = torch.zeros(ep, epr, dtype=torch.int32, device=dev)
+            send = torch.zeros(ep * C, d, dtype=x.dtype, device=dev)
+        # the counts travel in an all-to-all; only the device reads them
+        recv_counts = torch.empty(ep, epr, dtype=torch.int32, device=dev)
+        g.all_to_all(recv_counts, counts.contiguous())
+        recv = torch.empty(ep * C + S * T, d, dtype=x.dtype, device=dev)
+        g.all_to_all(recv[: ep * C], send)
+        for s in range(S):
+            recv[ep * C + s * T: ep * C + (s + 1) * T].copy_(x)
+        # segments: per source rank its local experts then a hole up to C rows; shared experts
+        rc = recv_counts.long()
+        seg_counts = torch.cat([rc, C - rc.sum(1, keepdim=True)], 1).flatten()
+        if S:
+            seg_counts = torch.cat([seg_counts, torch.full((S,), T, dtype=torch.long, device=dev)])
+        seg_offsets = torch.cat([torch.zeros(1, dtype=torch.long, device=dev),
+                                 torch.cumsum(seg_counts, 0)]).to(torch.int32)
+        out = be.experts(recv, seg_offsets, self._capacity_segments(dev), seg_counts.numel(),
+                         self.capacity_tokens)
+        ret = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
+        g.all_to_all(ret, out[: ep * C].contiguous() if S else out)
+        if T == 0:
+            return torch.empty(0, d, dtype=x.dtype, device=dev)
+        extra = out[ep * C:] if S else None
+        return be.combine(ret, p[pos.long()].to(torch.int32), w, T, extra, S)
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         x = hidden_states.reshape(-1, hidden_states.shape[-1])
+        if self.dispatch == "capacity":
+            return self._forward_capacity(x).view(hidden_states.shape)
         T, d = x.shape
         cfg, g, be = self.config, self.ep_group, self.backend
         ep, epr, k, S = g.ep_size, self.experts_per_rank, cfg.top_k, cfg.num_shared

@@ -37,7 +37,7 @@ class OracleExpertBackend:
         se = seg_expert.tolist()
         for i in range(num_seg):
             a, b = off[i], off[i + 1]
-            if b > a:
+            if b > a and se[i] != -1:   # -1: a hole (padding rows), skipped like the GEMMs do
                 e = se[i]
                 y = oracle.expert_mlp_ref(rows[a:b].numpy(), self.w1[e], self.w3[e], self.w2[e])
                 out[a:b] = torch.from_numpy(y)

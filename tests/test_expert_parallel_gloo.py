@@ -67,7 +67,8 @@ def _worker(rank, world, port, case, q):
         be = OracleExpertBackend(deq["w1"][idx], deq["w3"][idx], deq["w2"][idx], k, S)
         cfg = ExpertParallelConfig(num_experts=E, top_k=k, hidden_size=d, intermediate_size=F, ep_size=ep,
                                    group_size=g, num_shared=S)
-        layer = ExpertParallelW4A16Layer(cfg, grp, torch.from_numpy(gw), be, micro_batches=case.get("mb", 1))
+        layer = ExpertParallelW4A16Layer(cfg, grp, torch.from_numpy(gw), be, micro_batches=case.get("mb", 1),
+                                         dispatch=case.get("dispatch", "exact"), capacity_tokens=case.get("cap"))
         x = np.random.default_rng(100 + rank).standard_normal((Ts[rank], d), dtype=np.float32)
         if case.get("die") is not None and rank == case["die"]:
             be.route(torch.from_numpy(x), torch.from_numpy(gw), None)
@@ -113,6 +114,12 @@ def _run(world, case, timeout=120):
     (4, dict(E=64, S=2, k=6, d=64, F=64, g=64, T=[50, 9, 33, 20])),
     # two EP groups of two ranks inside a world of four (ranks 2, 3 are ranks 0, 1 of theirs)
     (4, dict(E=8, S=1, k=2, d=64, F=64, g=64, T=[20, 7, 13, 31], subgroups=True)),
+    # fixed-capacity dispatch (no host copy of the counts): ragged and empty token counts,
+    # shared experts, a rank receiving nothing, fine-grained routing
+    (2, dict(E=8, S=0, k=2, d=64, F=64, g=64, T=[16, 16], dispatch="capacity", cap=16)),
+    (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[5, 17], dispatch="capacity", cap=24)),
+    (4, dict(E=8, S=0, k=3, d=64, F=64, g=64, T=[30, 0, 12, 1], dispatch="capacity", cap=32)),
+    (4, dict(E=64, S=2, k=6, d=64, F=64, g=64, T=[9, 3, 8, 2], dispatch="capacity", cap=9)),
 ])
 def test_expert_parallel_matches_single_process(world, case):
     results, codes = _run(world, case)

@@ -1,6 +1,8 @@
 """Expert-parallel layer on GPUs (NCCL): each rank's output must match the single-GPU layer
 on the same tokens with the full expert set (max relative error 1e-2, the layer bar).
-Runs with world size 1 on any box, and with world size 2 when two GPUs are visible."""
+Runs with world size 1 on any box, and with world size 2 when two GPUs are visible.
+The fixed-capacity dispatch (no host copy of the counts) is also captured in a CUDA graph
+and replayed: the replay must reproduce the eager output bit for bit."""
 import os
 import socket
 import sys
@@ -40,7 +42,9 @@ def _worker(rank, world, port, case, q):
         shared = [(w1[E + s], w3[E + s], w2[E + s]) for s in range(S)] or None
         ex = W4A16Experts.from_dense(w1[:E], w3[:E], w2[:E], g, shared=shared)
         bias = torch.linspace(-1, 1, E, device=dev) if case.get("bias") else None
-        ep_layer = ExpertParallelW4A16Layer.from_full(gw, ex, k, gate_bias=bias, micro_batches=case.get("mb", 1))
+        ep_layer = ExpertParallelW4A16Layer.from_full(gw, ex, k, gate_bias=bias, micro_batches=case.get("mb", 1),
+                                                      dispatch=case.get("dispatch", "exact"),
+                                                      capacity_tokens=case.get("cap"))
         ref_layer = W4A16MoELayer(gw, ex, k, gate_bias=bias)
         T = case["T"][rank]
         x = torch.randn(T, d, generator=torch.Generator(device="cpu").manual_seed(10 + rank)).to(torch.bfloat16).to(dev)
@@ -49,6 +53,21 @@ def _worker(rank, world, port, case, q):
         y_ref = ref_layer(x)
         torch.cuda.synchronize()
         err = ((y.float() - y_ref.float()).abs().max() / y_ref.float().abs().max()).item()
+        if case.get("dispatch") == "capacity":
+            # the whole step (router, gather, three all-to-alls, GEMMs, combine) in one graph
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                ep_layer(x)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                y_graph = ep_layer(x)
+            graph.replay()
+            torch.cuda.synchronize()
+            if not torch.equal(y_graph, y):
+                err = float("inf")
+            del graph, y_graph
         q.put((rank, "ok", err))
         dist.barrier()
         dist.destroy_process_group()
@@ -80,7 +99,10 @@ CASES = [dict(E=8, S=0, k=2, d=512, F=256, g=128, T=[300, 77]),
          dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64]),
          # micro-batched dispatch / combine (one rank with an empty micro-batch)
          dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[2000, 1], mb=2),
-         dict(E=16, S=0, k=4, d=256, F=128, g=64, T=[333, 150], mb=3)]
+         dict(E=16, S=0, k=4, d=256, F=128, g=64, T=[333, 150], mb=3),
+         # fixed-capacity dispatch: Mixtral decode shape, and shared experts with ragged tokens
+         dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64], dispatch="capacity", cap=64),
+         dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="capacity", cap=40)]
 
 
 @pytest.mark.parametrize("case", CASES)
