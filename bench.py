@@ -379,6 +379,53 @@ def cpu_baseline(ex, gw, tokens, seconds_budget=20.0):
 
 
 # ----------------------------------------------------------------------------- arms
+def measure_decode(args, x, gw, ex, layer, ws, stream, barrier, peaks, peak_kind, device):
+    """Decode step (64 tokens per GPU), on every rank.  One GPU: the single-GPU layer; N GPUs:
+    the expert-parallel layer with fixed-capacity dispatch (no host synchronisation).  The
+    step is timed eagerly and as a CUDA graph replay (how a serving loop runs decode); the
+    reported step time is the replay's, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from light_moe_b200.layer import W4A16MoELayer
+    xd = x[:T_DECODE].contiguous()
+    check = None
+    if ws > 1:
+        from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
+        dlayer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, dispatch="capacity",
+                                                    capacity_tokens=T_DECODE)
+        y_ep = dlayer(xd)
+        y_one = W4A16MoELayer(gw, ex, TOPK)(xd)
+        rel = ((y_ep.float() - y_one.float()).abs().max() / y_one.float().abs().max()).double().reshape(1)
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
+        check = float(rel.item())
+        dfwd = dlayer.forward
+    else:
+        dfwd = layer.forward
+    dsteps = max(args.steps, 20)
+    eager = time_device(lambda: dfwd(xd), dsteps, args.warmup, stream, barrier) / dsteps
+    if barrier:
+        barrier()
+    graph = time_graph(lambda: dfwd(xd), 10, max(2, dsteps // 10), stream)
+    t = torch.tensor([eager, graph], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    eager, graph = float(t[0]), float(t[1])
+    wbytes = (ex.w13_packed.numel() + ex.w2_packed.numel()) / ws
+    layer_gbs = wbytes / graph / 1e9
+    out = {"tokens_per_gpu": T_DECODE, "value": round(T_DECODE * ws / graph, 1), "unit": "tokens/s",
+           "ms_per_step": round(graph * 1e3, 4), "eager_ms_per_step": round(eager * 1e3, 4),
+           "timing": "CUDA graph replay of 10 steps (max over ranks); eager: back-to-back calls",
+           "dispatch": "fixed-capacity all-to-all, no host synchronisation" if ws > 1 else "single GPU",
+           "layer_weight_stream_gbs_per_gpu": round(layer_gbs, 1),
+           "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4)}
+    if ws > 1:
+        out["ep_max_rel_err"] = check
+    else:
+        out["roofline_gate_up"] = gemm_roofline(xd, gw, ex, T_DECODE, stream, peaks, peak_kind)
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -472,26 +519,13 @@ def run_ours(args):
                    "algorithmic": {"flops": 2.0 * g_rows * (2 * FFN) * D}, "traffic": None,
                    "traffic_unit": "DRAM bytes per launch (ncu); not captured for the per-rank launch"}
 
+    decode_all = measure_decode(args, x, gw, ex, layer if ws == 1 else None, ws, stream, barrier, peaks, peak_kind,
+                                device)
+
     result = None
     if rank == 0:
         roof = roof_ep if ws > 1 else gemm_roofline(x, gw, ex, T, stream, peaks, peak_kind)
-        # decode sub-measurement (64 tokens per GPU)
-        xd = x[:T_DECODE].contiguous()
-        if ws > 1:
-            dsecs = None
-        else:
-            dsecs = time_device(lambda: fwd(xd), max(args.steps, 20), args.warmup, stream)
-        decode = None
-        if dsecs is not None:
-            dsteps = max(args.steps, 20)
-            droof = gemm_roofline(xd, gw, ex, T_DECODE, stream, peaks, peak_kind)
-            wbytes = ex.w13_packed.numel() + ex.w2_packed.numel()
-            layer_gbs = wbytes / (dsecs / dsteps) / 1e9
-            decode = {"tokens": T_DECODE, "value": round(T_DECODE * dsteps / dsecs, 1), "unit": "tokens/s",
-                      "ms_per_step": round(dsecs / dsteps * 1e3, 4),
-                      "layer_weight_stream_gbs": round(layer_gbs, 1),
-                      "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4),
-                      "roofline_gate_up": droof}
+        decode = decode_all
         extra = None
         if ws == 1 and not args.no_extra:
             try:
@@ -580,6 +614,42 @@ def run_reference(args):
     return res
 
 
+KERNEL_CASES = ("router-e8", "router-e64", "gateup-t8192", "down-t8192", "decode-gateup-t64", "decode-down-t64")
+
+
+def run_kernel_case(args):
+    """One kernel of the path, launched `steps` times on the bench's inputs (for profiler
+    captures of a single kernel; prints the CUDA-event time per launch)."""
+    import torch
+
+    from light_moe_b200 import ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream()
+    case = args.kernel_case
+    if case.startswith("router"):
+        e, k = (8, 2) if case == "router-e8" else (64, 6)
+        g = torch.Generator(device=device).manual_seed(0)
+        x = torch.randn(16384, D, generator=g, device=device).to(torch.bfloat16)
+        w = (torch.randn(e, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        fn = lambda: ops.fused_gate_topk_ex(x, w, k)   # noqa: E731
+    else:
+        T = 8192 if case.endswith("t8192") else T_DECODE
+        x, gw, ex = make_problem(T, device, seed=0)
+        ids, wts, counts, offsets, sidx = ops.fused_gate_topk_ex(x, gw, TOPK)[:5]
+        xp = x[(sidx // TOPK).long()].contiguous()
+        h = ops.w4a16_grouped_gemm(xp, ex.w13_packed, offsets, E, 2 * FFN, GROUP, 1, None, None, 0, T)
+        if "gateup" in case:
+            fn = lambda: ops.w4a16_grouped_gemm(xp, ex.w13_packed, offsets, E, 2 * FFN, GROUP, 1,  # noqa: E731
+                                                None, None, 0, T)
+        else:
+            fn = lambda: ops.w4a16_grouped_gemm(h, ex.w2_packed, offsets, E, D, GROUP, 0,  # noqa: E731
+                                                None, None, 0, T)
+    secs = time_device(fn, args.steps, args.warmup, stream) / args.steps
+    print(json.dumps({"kernel_case": case, "launches": args.steps + args.warmup, "us_per_launch": round(secs * 1e6, 1)}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -592,10 +662,14 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the router / skewed-GEMM / fine-grained measurements")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="expert-parallel runs: micro-batches whose all-to-alls overlap the GEMMs")
+    ap.add_argument("--kernel-case", choices=KERNEL_CASES, default=None,
+                    help="launch one kernel of the path `steps` times (profiler captures) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.kernel_case:
+        run_kernel_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -32,10 +32,12 @@ With ``dispatch="capacity"`` (decode: small batches of at most ``capacity_tokens
 per rank, the same bound on every rank) nothing is copied to the host: every rank sends
 every other rank a fixed block of C = capacity_tokens * top_k rows (its rows for that rank,
 then padding), so both all-to-alls have equal, host-known splits; the per-(rank, expert)
-counts still travel in a small all-to-all, but only the device reads them -- the segment
-offsets are prefix sums on the device, each source rank's padding is a "hole" segment
-(weight matrix -1, skipped by the GEMMs), and the combine reads the returned block through
-the padded positions of the rank's own sorted rows.  The whole step can be captured in a
+counts still travel in a small all-to-all, but only the device reads them: the received
+rows are regrouped expert-major by a device-computed permutation (so each local expert's
+weights stream once), the segment offsets are prefix sums on the device, the padding of
+all source ranks is one "hole" segment (weight matrix -1, skipped by the GEMMs), and the
+combine reads the returned block through the padded positions of the rank's own sorted
+rows.  The whole step can be captured in a
 CUDA graph.  The reference pads to equal splits as well (expert_parallel.py:186-244) but
 sends every token to every rank; here only the routed rows carry data.
 
@@ -152,6 +154,14 @@ class CudaExpertBackend:
                   self.top_k, rows.data_ptr(), capi.stream_handle())
         return rows
 
+    def take(self, rows, index):
+        """rows[index] (int32 index on the device) with the library's row gather."""
+        from . import capi
+        out = torch.empty(index.numel(), rows.shape[1], dtype=rows.dtype, device=rows.device)
+        capi.call("lmoe_permute_rows", rows.data_ptr(), rows.element_size(), index.data_ptr(), index.numel(),
+                  rows.shape[1], 1, out.data_ptr(), capi.stream_handle())
+        return out
+
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         e = self.ex
         if self.gemm_timer is not None:
@@ -224,8 +234,8 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
     def _capacity_segments(self, device):
         key = ("cap", str(device))
         if key not in self._seg_cache:
-            ep, epr, S = self.ep_group.ep_size, self.experts_per_rank, self.config.num_shared
-            seg = [e if e < epr else -1 for _ in range(ep) for e in range(epr + 1)] + [epr + s for s in range(S)]
+            epr, S = self.experts_per_rank, self.config.num_shared
+            seg = list(range(epr)) + [-1] + [epr + s for s in range(S)]
             self._seg_cache[key] = torch.tensor(seg, dtype=torch.int32, device=device)
         return self._seg_cache[key]
 
@@ -259,24 +269,40 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         # the counts travel in an all-to-all; only the device reads them
         recv_counts = torch.empty(ep, epr, dtype=torch.int32, device=dev)
         g.all_to_all(recv_counts, counts.contiguous())
-        recv = torch.empty(ep * C + S * T, d, dtype=x.dtype, device=dev)
-        g.all_to_all(recv[: ep * C], send)
-        for s in range(S):
-            recv[ep * C + s * T: ep * C + (s + 1) * T].copy_(x)
-        # segments: per source rank its local experts then a hole up to C rows; shared experts
+        recv = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
+        g.all_to_all(recv, send)
+        # regroup the received rows expert-major (each local expert one segment, so its
+        # weights stream once whatever the number of source ranks): g[j] = the received row
+        # at expert-major position j; every source's padding becomes one trailing hole, so
+        # g is a permutation of the ep * C rows and its inverse is a scatter
         rc = recv_counts.long()
-        seg_counts = torch.cat([rc, C - rc.sum(1, keepdim=True)], 1).flatten()
+        cnt = torch.cat([rc, C - rc.sum(1, keepdim=True)], 1)                        # [ep, epr + 1]
+        src_start = (torch.arange(ep, device=dev) * C)[:, None] + torch.cumsum(cnt, 1) - cnt
+        cnt_em = cnt.t().contiguous().flatten()                                       # (expert, source)
+        dst_start = torch.cumsum(cnt_em, 0) - cnt_em
+        jj = torch.arange(ep * C, device=dev)
+        kk = torch.searchsorted(dst_start, jj, right=True) - 1
+        g_idx = src_start.t().contiguous().flatten()[kk] + (jj - dst_start[kk])
+        inv = torch.empty_like(g_idx)
+        inv[g_idx] = jj
+        rows_em = torch.empty(ep * C + S * T, d, dtype=x.dtype, device=dev)
+        rows_em[: ep * C] = be.take(recv, g_idx.to(torch.int32))
+        for s in range(S):
+            rows_em[ep * C + s * T: ep * C + (s + 1) * T].copy_(x)
+        # segments: the local experts, the padding hole, the shared experts on local tokens
+        seg_counts = cnt_em.view(epr + 1, ep).sum(1)
         if S:
             seg_counts = torch.cat([seg_counts, torch.full((S,), T, dtype=torch.long, device=dev)])
         seg_offsets = torch.cat([torch.zeros(1, dtype=torch.long, device=dev),
                                  torch.cumsum(seg_counts, 0)]).to(torch.int32)
-        out = be.experts(recv, seg_offsets, self._capacity_segments(dev), seg_counts.numel(),
-                         self.capacity_tokens)
+        out_em = be.experts(rows_em, seg_offsets, self._capacity_segments(dev), seg_counts.numel(),
+                            self.capacity_tokens)
+        out = be.take(out_em, inv.to(torch.int32))                                     # back to capacity order
         ret = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
-        g.all_to_all(ret, out[: ep * C].contiguous() if S else out)
+        g.all_to_all(ret, out)
+        extra = out_em[ep * C:] if S else None
         if T == 0:
             return torch.empty(0, d, dtype=x.dtype, device=dev)
-        extra = out[ep * C:] if S else None
         return be.combine(ret, p[pos.long()].to(torch.int32), w, T, extra, S)
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:

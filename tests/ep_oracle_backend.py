@@ -31,6 +31,9 @@ class OracleExpertBackend:
     def gather(self, x, sorted_idx):
         return x[(sorted_idx // self.top_k).long()].contiguous()
 
+    def take(self, rows, index):
+        return rows[index.long()].contiguous()
+
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         out = torch.zeros(rows.shape[0], self.w2.shape[1], dtype=rows.dtype)
         off = seg_offsets.tolist()
