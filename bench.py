@@ -448,7 +448,8 @@ def run_ours(args):
     x, gw, ex = make_problem(T, device, seed=0)
     if ws > 1:
         from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
-        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, micro_batches=args.micro_batches)
+        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, micro_batches=args.micro_batches,
+                                                   sm_reserve=args.sm_reserve)
         fwd = layer.forward
         launches_per_step = 5 * layer.micro_batches
     else:
@@ -545,6 +546,7 @@ def run_ours(args):
                        "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP,
                        "parallelism": f"ep{ws}" if ws > 1 else "single GPU",
                        "ep_micro_batches": args.micro_batches if ws > 1 else None,
+                       "ep_sm_reserve": layer.sm_reserve if ws > 1 else None,
                        "l2": l2_note(ex, ws, T)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                     "d2h_bytes_per_step": T * D * 2,
@@ -662,6 +664,9 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the router / skewed-GEMM / fine-grained measurements")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="expert-parallel runs: micro-batches whose all-to-alls overlap the GEMMs")
+    ap.add_argument("--sm-reserve", type=int, default=None,
+                    help="expert-parallel runs: SMs the GEMMs leave to the all-to-alls (default 16 with "
+                         "several micro-batches, else 0)")
     ap.add_argument("--kernel-case", choices=KERNEL_CASES, default=None,
                     help="launch one kernel of the path `steps` times (profiler captures) and exit")
     args = ap.parse_args()

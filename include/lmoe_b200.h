@@ -46,6 +46,13 @@ const char* lmoe_status_string(int status);
  * `stream`).  0 means no kernel reported a problem. */
 int lmoe_read_error(const void* workspace, uint32_t* out, lmoe_stream_t stream);
 
+/* Caps the number of CTAs (one per SM) of the persistent grouped GEMMs launched afterwards
+ * by this process (0 = no cap: one per SM).  Leaving SMs free lets kernels on other streams
+ * -- NCCL's all-to-all of the next micro-batch -- run beside a GEMM instead of after it.
+ * Process-wide; read at each launch.  New (the reference has no persistent kernels). */
+int lmoe_set_gemm_sm_limit(int max_ctas);
+int lmoe_get_gemm_sm_limit(void);
+
 /* ------------------------------------------------------------------------------------ */
 /* Router: gate logits + fp32 softmax + top-k + renormalise + histogram / offsets /       */
 /* stable permutation, in one kernel.                                                     */

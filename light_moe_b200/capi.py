@@ -33,6 +33,8 @@ SIGNATURES = {
     "lmoe_version": (_I, []),
     "lmoe_status_string": (ctypes.c_char_p, [_I]),
     "lmoe_read_error": (_I, [_P, _P, _P]),
+    "lmoe_set_gemm_sm_limit": (_I, [_I]),
+    "lmoe_get_gemm_sm_limit": (_I, []),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),
     "lmoe_fused_gate_topk_typed": (_I, [_P, _I, _P, _I, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,

@@ -620,8 +620,9 @@ int run_decode_gemm(const DecodeProblem& p, cudaStream_t stream) {
   st = encode_tmap_kblocks(&tm_x32, p.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.total_rows, (uint64_t)p.K,
                            (uint64_t)p.ldx * 2, 32, 2);
   if (st != LMOE_OK) return st;
-  if (w4_scale_groups(g) == 2) return launch_decode<2>(tm_x16, tm_x32, a, dev.num_sms, stream);
-  return launch_decode<1>(tm_x16, tm_x32, a, dev.num_sms, stream);
+  const int grid = gemm_grid(dev);
+  if (w4_scale_groups(g) == 2) return launch_decode<2>(tm_x16, tm_x32, a, grid, stream);
+  return launch_decode<1>(tm_x16, tm_x32, a, grid, stream);
 }
 
 }  // namespace lmoe

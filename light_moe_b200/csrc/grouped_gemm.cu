@@ -704,7 +704,7 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   } else {
     tm_w = tm_x;
   }
-  const int grid = dev.num_sms;
+  const int grid = gemm_grid(dev);
   if (w4) {
     //                          BN  DQ WST BST AST ACC  W4   BOX
     if (small) return launch_gemm<64, 16, 12, 6, 4, 2, true, 16>(tm_x, tm_w, a, grid, stream);

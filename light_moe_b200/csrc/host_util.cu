@@ -1,6 +1,7 @@
 // host_util.cu -- device-info cache, TMA descriptor encoding and the small C-ABI utilities.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "host_util.h"
@@ -41,6 +42,15 @@ int current_context_id(unsigned long long* id) {
   if (g_ctx_id(ctx, &v) != CUDA_SUCCESS) return LMOE_ERR_DEVICE;
   *id = v;
   return LMOE_OK;
+}
+
+namespace {
+std::atomic<int> g_gemm_sm_limit{0};
+}  // namespace
+
+int gemm_grid(const DeviceInfo& dev) {
+  const int cap = g_gemm_sm_limit.load(std::memory_order_relaxed);
+  return cap > 0 && cap < dev.num_sms ? cap : dev.num_sms;
 }
 
 int get_device_info(DeviceInfo* out) {
@@ -163,6 +173,14 @@ extern "C" const char* lmoe_status_string(int status) {
   if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
   return "unknown status";
 }
+
+extern "C" int lmoe_set_gemm_sm_limit(int max_ctas) {
+  if (max_ctas < 0) return LMOE_ERR_INVALID_ARG;
+  lmoe::g_gemm_sm_limit.store(max_ctas, std::memory_order_relaxed);
+  return LMOE_OK;
+}
+
+extern "C" int lmoe_get_gemm_sm_limit(void) { return lmoe::g_gemm_sm_limit.load(std::memory_order_relaxed); }
 
 extern "C" int lmoe_read_error(const void* workspace, uint32_t* out, lmoe_stream_t stream) {
   if (!workspace || !out) return LMOE_ERR_INVALID_ARG;

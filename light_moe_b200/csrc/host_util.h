@@ -37,6 +37,9 @@ struct DeviceInfo {
 
 int get_device_info(DeviceInfo* out);
 
+// CTAs of a persistent GEMM launch: one per SM, capped by lmoe_set_gemm_sm_limit.
+int gemm_grid(const DeviceInfo& dev);
+
 // Process-unique id of the calling thread's current CUDA context (cuCtxGetId); 0 when no
 // context is bound to the thread yet.
 int current_context_id(unsigned long long* id);

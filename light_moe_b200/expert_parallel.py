@@ -141,6 +141,9 @@ class CudaExpertBackend:
         # when a list, every gate/up GEMM appends (start event, end event, rows) on the current
         # stream (used to time the per-rank kernel inside an expert-parallel step)
         self.gemm_timer = None
+        # CTAs of the persistent GEMMs (None: one per SM); fewer leave SMs to the all-to-all
+        # kernels of other micro-batches running beside the GEMMs
+        self.sm_limit = None
 
     def route(self, x, gate_weight, gate_bias):
         ids, w, counts, offsets, sidx, pos = ops.fused_gate_topk_ex(x, gate_weight, self.top_k, gate_bias)[:6]
@@ -163,6 +166,17 @@ class CudaExpertBackend:
         return out
 
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+        if self.sm_limit is None:
+            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows)
+        from . import capi
+        prev = capi.lib().lmoe_get_gemm_sm_limit()
+        capi.call("lmoe_set_gemm_sm_limit", int(self.sm_limit))
+        try:
+            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows)
+        finally:
+            capi.call("lmoe_set_gemm_sm_limit", prev)
+
+    def _experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         e = self.ex
         if self.gemm_timer is not None:
             ev0 = torch.cuda.Event(enable_timing=True)
@@ -185,7 +199,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
 
     def __init__(self, config: ExpertParallelConfig, ep_group: ExpertParallelGroup, gate_weight: torch.Tensor,
                  backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1,
-                 dispatch: str = "exact", capacity_tokens: Optional[int] = None):
+                 dispatch: str = "exact", capacity_tokens: Optional[int] = None, sm_reserve: Optional[int] = None):
         super().__init__()
         if dispatch not in ("exact", "capacity"):
             raise ValueError(f"dispatch must be 'exact' or 'capacity', not {dispatch!r}")
@@ -202,6 +216,12 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         self.local_expert_start = ep_group.rank * self.experts_per_rank
         self.local_expert_end = self.local_expert_start + self.experts_per_rank
         self.micro_batches = max(1, int(micro_batches))   # must be equal on all ranks
+        # SMs left free by the GEMMs while micro-batches overlap (default 16 with more than
+        # one micro-batch, 0 otherwise)
+        self.sm_reserve = (16 if self.micro_batches > 1 else 0) if sm_reserve is None else int(sm_reserve)
+        if self.sm_reserve > 0 and hasattr(backend, "sm_limit") and torch.cuda.is_available():
+            props = torch.cuda.get_device_properties(torch.cuda.current_device())
+            backend.sm_limit = max(1, props.multi_processor_count - self.sm_reserve)
         # kernels of ours per forward: router, gather, gate/up GEMM, down GEMM, combine per
         # micro-batch (set by the last forward)
         self.kernels_per_step = 5
@@ -210,7 +230,8 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
     @classmethod
     def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
                   group: Optional[dist.ProcessGroup] = None, gate_bias: Optional[torch.Tensor] = None,
-                  micro_batches: int = 1, dispatch: str = "exact", capacity_tokens: Optional[int] = None):
+                  micro_batches: int = 1, dispatch: str = "exact", capacity_tokens: Optional[int] = None,
+                  sm_reserve: Optional[int] = None):
         """Build this rank's layer from the full (all-expert) prepacked weights."""
         ws = dist.get_world_size(group)
         g = ExpertParallelGroup(ws).attach(group)
@@ -221,7 +242,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
                                    num_shared=experts.num_shared)
         local = slice_experts(experts, g.rank * cfg.experts_per_rank, (g.rank + 1) * cfg.experts_per_rank)
         return cls(cfg, g, gate_weight.to(torch.bfloat16).contiguous(), CudaExpertBackend(local, top_k), gate_bias,
-                   micro_batches, dispatch, capacity_tokens)
+                   micro_batches, dispatch, capacity_tokens, sm_reserve)
 
     def _segments(self, device):
         key = (str(device),)

@@ -88,3 +88,15 @@ def test_layer_rejects_bad_arguments_without_gpu():
     assert st == capi.LMOE_ERR_INVALID_ARG
     with pytest.raises(capi.LmoeError):
         capi.call("lmoe_combine_rows", None, None, None, 4, 2, 7, None, 0, None, None)
+
+
+def test_gemm_sm_limit_is_process_wide_and_validated():
+    lib = capi.lib()
+    prev = lib.lmoe_get_gemm_sm_limit()
+    try:
+        assert lib.lmoe_set_gemm_sm_limit(132) == 0 and lib.lmoe_get_gemm_sm_limit() == 132
+        assert lib.lmoe_set_gemm_sm_limit(-1) == capi.LMOE_ERR_INVALID_ARG
+        assert lib.lmoe_get_gemm_sm_limit() == 132
+        assert lib.lmoe_set_gemm_sm_limit(0) == 0 and lib.lmoe_get_gemm_sm_limit() == 0
+    finally:
+        lib.lmoe_set_gemm_sm_limit(prev)

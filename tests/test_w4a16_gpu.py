@@ -118,6 +118,31 @@ def test_w4_gemm_plain(counts, hint):
     _assert_close(y, _ref_plain(x, deq, off))
 
 
+@pytest.mark.parametrize("hint", [0, 64])
+def test_w4_gemm_hole_segments(hint):
+    """Segments mapped to weight matrix -1 (the padding of a fixed-capacity exchange) are
+    skipped without an error and their output rows are left untouched; the other segments
+    use their mapped matrices (several segments may share one)."""
+    E, N, K, g = 3, 256, 512, 128
+    packed, deq = _expert_setup(E, N, K, g, seed=77)
+    counts = [9, 30, 16, 0, 12, 40]
+    seg_w = [2, -1, 0, -1, 2, -1]
+    R = sum(counts)
+    x = _w((R, K), seed=3, scale=1.0)
+    off = _offsets(counts)
+    se = torch.tensor(seg_w, dtype=torch.int32, device="cuda")
+    y = w4_gemm(x, packed, N, g, off, hint=hint, seg_expert=se)
+    o = off.cpu().tolist()
+    ref = torch.zeros(R, N, device="cuda")
+    for i, w in enumerate(seg_w):
+        if w >= 0 and counts[i]:
+            ref[o[i]:o[i + 1]] = x[o[i]:o[i + 1]].float() @ deq[w].T
+    _assert_close(y, ref)
+    for i, w in enumerate(seg_w):
+        if w < 0:
+            assert torch.all(y[o[i]:o[i + 1]] == 0), "a hole's output rows were written"
+
+
 def test_w4_gemm_many_experts_int64_offsets():
     rng = np.random.default_rng(0)
     E = 64
