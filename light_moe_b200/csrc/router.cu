@@ -99,6 +99,104 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Permutation phase when every CTA routed exactly one tile (tile = blockIdx.x): the tile's
+// expert ids and per-expert row bitmaps are still in shared memory, so only the
+// [num_tiles, E] count table is read back.  Per expert, a warp sums the counts of the tiles
+// before this one and of all tiles (lanes over tiles, then a shuffle reduction: integer
+// sums, order-exact); then the exclusive scan of the totals and the scatter of the tile's
+// tokens, as in perm_phase.  `area` holds the count table and the prefixes (16-byte aligned)
+// below the tile's ids.
+template <int KMAX, int NT>
+__device__ __forceinline__ void perm_phase_one_tile(const RouterArgs& a, int32_t* area, const int32_t* tile_ids,
+                                                    const uint32_t* bits, int32_t* total, int32_t* offs) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int tile = (int)blockIdx.x;
+  const int n = a.num_tiles * a.E;
+  // all of a thread's 16-byte loads in flight at once (one L2 round trip for the table)
+  constexpr int kBatch = 8;
+  for (int i0 = tid * 4; i0 < n; i0 += NT * 4 * kBatch) {
+    int4 v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * NT * 4;
+      if (i + 3 < n) v[u] = __ldcg(reinterpret_cast<const int4*>(a.tile_counts + i));
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * NT * 4;
+      if (i + 3 < n) {
+        *reinterpret_cast<int4*>(area + i) = v[u];
+      } else {
+        for (int r = i; r < n; ++r) area[r] = __ldcg(a.tile_counts + r);   // ragged tail
+      }
+    }
+  }
+  __syncthreads();
+  int32_t* pref = area + ((n + 3) & ~3);   // [E] counts of this expert in the tiles before this one
+  for (int e = warp; e < a.E; e += NT / 32) {
+    int32_t before = 0, all = 0;
+    for (int tt = lane; tt < a.num_tiles; tt += 32) {
+      const int32_t c = area[tt * a.E + e];
+      all += c;
+      if (tt < tile) before += c;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+    }
+    if (lane == 0) {
+      pref[e] = before;
+      total[e] = all;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int32_t run = 0;
+    for (int e0 = 0; e0 < a.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int32_t c = e < a.E ? total[e] : 0;
+      const int32_t v = warp_inclusive_scan(c, lane);
+      if (e < a.E) offs[e] = run + v - c;
+      run += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) offs[a.E] = run;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = tid; e < a.E; e += NT) {
+      a.counts[e] = total[e];
+      a.offsets[e] = offs[e];
+    }
+    if (tid == 0) a.offsets[a.E] = offs[a.E];
+  }
+  for (int row = tid; row < a.bm; row += NT) {
+    const int64_t t = (int64_t)tile * a.bm + row;
+    if (t >= a.T) continue;
+    const int w = row >> 5;
+    const uint32_t below = (1u << (row & 31)) - 1u;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < a.k) {
+        const int e = tile_ids[row * KMAX + j];
+        int rank = __popc(bits[e * 4 + w] & below);
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+          if (i < w) rank += __popc(bits[e * 4 + i]);
+        const int32_t pos = offs[e] + pref[e] + rank;
+        a.sorted_idx[pos] = (int32_t)(t * a.k + j);
+        if (a.positions) a.positions[t * a.k + j] = pos;
+      }
+    }
+  }
+}
+
 // Permutation phase, run once every tile's counts and bitmaps are in global memory: the
 // per-expert totals and, for each tile this CTA owns (blockIdx.x + i * gridDim.x), the
 // count of earlier tiles, from the [num_tiles, E] count table staged through shared memory
@@ -240,6 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nk = (a.d + kBK * kBoxes - 1) / (kBK * kBoxes);   // stages per tile
+  // Every CTA routes at most one tile: after its accumulator is full the stage area is free,
+  // so the epilogue keeps the tile's expert ids at its end (and the bitmap in the header) for
+  // the permutation phase, which then reads back only the count table.
+  const int area_ints = (int)(((size_t)a.stages * a.stage_bytes) / 4);
+  const bool one_tile = a.num_tiles <= (int)gridDim.x &&
+                        ((a.num_tiles * a.E + 3) & ~3) + a.E + kBM * KMAX <= area_ints;
+  int32_t* tile_ids = reinterpret_cast<int32_t*>(base) + area_ints - kBM * KMAX;   // [row][KMAX]
   constexpr uint32_t kXBox = kBM * kBK * 2;
 
   if (tid == 0) {
@@ -366,91 +471,126 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row < a.bm && t < a.T;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * a.Epad;
       uint32_t r[16];
-      // pass 1: logits (+bias), running max over this thread's chunks
-      float m = -INFINITY;
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        tmem_ld16(taddr + c0, r);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = c0 + i;
-          if (e < a.E) {
-            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
-            m = fmaxf(m, l);
-            if (a.logits && valid) a.logits[t * a.E + e] = l;
-          }
-        }
-      }
-      if (split) {   // the maximum is exact in any order
-        x_m[(owner ? 0 : kBM) + row] = m;
-        named_bar_sync(pair_bar, 64);
-        m = fmaxf(x_m[row], x_m[kBM + row]);
-      }
-      // pass 2: exp(l - max) of this thread's chunks, written back over the logits
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        tmem_ld16(taddr + c0, r);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = c0 + i;
-          const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e < a.E ? e : 0]);
-          r[i] = e < a.E ? __float_as_uint(softmax_exp(__fsub_rn(l, m))) : 0u;
-        }
-        tmem_st16(taddr + c0, r);
-      }
-      tmem_wait_st();
-      if (split) {
-        tc_fence_before();
-        named_bar_sync(pair_bar, 64);
-        tc_fence_after();
-      }
-      // the owner sums all exponentials sequentially over experts 0..E-1
-      float inv = 0.0f;
-      if (owner) {
-        float sum = 0.0f;
-        for (int c0 = 0; c0 < a.Epad; c0 += 16) {
-          tmem_ld16(taddr + c0, r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (c0 + i < a.E) sum = __fadd_rn(sum, __uint_as_float(r[i]));
-        }
-        inv = __frcp_rn(sum);
-      }
-      if (split) {
-        if (owner) x_inv[row] = inv;
-        named_bar_sync(pair_bar, 64);
-        if (!owner) inv = x_inv[row];
-      }
-      // pass 3: probabilities and top-k over this thread's chunks
       float tv[KMAX];
       int ti[KMAX];
 #pragma unroll
       for (int j = 0; j < KMAX; ++j) { tv[j] = -INFINITY; ti[j] = 0; }
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        tmem_ld16(taddr + c0, r);
+      if (!split) {
+        // one 16-column chunk per row: one tensor-memory load, everything else in registers
+        // (the same operations in the same order as the chunked passes below)
+        tmem_ld16(taddr, r);
+        float v[16];
+        float m = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int e = c0 + i;
-          if (e < a.E) {
-            const float p = __fmul_rn(__uint_as_float(r[i]), inv);
-            if (a.probs && valid) a.probs[t * a.E + e] = p;
-            topk_insert<KMAX>(tv, ti, p, e);
+          v[i] = 0.0f;
+          if (i < a.E) {
+            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[i]);
+            v[i] = l;
+            m = fmaxf(m, l);
+            if (a.logits && valid) a.logits[t * a.E + i] = l;
           }
         }
-      }
-      if (split) {
-        // the helper's list (higher expert ids, descending) is inserted after the owner's:
-        // the merged list equals the sequential insertion over all experts
-        tc_fence_before();
-        if (!owner) {
+        float sum = 0.0f;
 #pragma unroll
-          for (int j = 0; j < KMAX; ++j) {
-            x_tv[j * kBM + row] = tv[j];
-            x_ti[j * kBM + row] = ti[j];
+        for (int i = 0; i < 16; ++i) {
+          if (i < a.E) {
+            v[i] = softmax_exp(__fsub_rn(v[i], m));
+            sum = __fadd_rn(sum, v[i]);
           }
         }
-        named_bar_sync(pair_bar, 64);
+        const float inv = __frcp_rn(sum);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (i < a.E) {
+            const float p = __fmul_rn(v[i], inv);
+            if (a.probs && valid) a.probs[t * a.E + i] = p;
+            topk_insert<KMAX>(tv, ti, p, i);
+          }
+        }
+      } else {
+        // pass 1: logits (+bias), running max over this thread's chunks
+        float m = -INFINITY;
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          tmem_ld16(taddr + c0, r);
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int e = c0 + i;
+            if (e < a.E) {
+              const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e]);
+              m = fmaxf(m, l);
+              if (a.logits && valid) a.logits[t * a.E + e] = l;
+            }
+          }
+        }
+        if (split) {   // the maximum is exact in any order
+          x_m[(owner ? 0 : kBM) + row] = m;
+          named_bar_sync(pair_bar, 64);
+          m = fmaxf(x_m[row], x_m[kBM + row]);
+        }
+        // pass 2: exp(l - max) of this thread's chunks, written back over the logits
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          tmem_ld16(taddr + c0, r);
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int e = c0 + i;
+            const float l = __fadd_rn(__uint_as_float(r[i]), h->bias[e < a.E ? e : 0]);
+            r[i] = e < a.E ? __float_as_uint(softmax_exp(__fsub_rn(l, m))) : 0u;
+          }
+          tmem_st16(taddr + c0, r);
+        }
+        tmem_wait_st();
+        if (split) {
+          tc_fence_before();
+          named_bar_sync(pair_bar, 64);
+          tc_fence_after();
+        }
+        // the owner sums all exponentials sequentially over experts 0..E-1
+        float inv = 0.0f;
         if (owner) {
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j) topk_insert<KMAX>(tv, ti, x_tv[j * kBM + row], x_ti[j * kBM + row]);
+          float sum = 0.0f;
+          for (int c0 = 0; c0 < a.Epad; c0 += 16) {
+            tmem_ld16(taddr + c0, r);
+  #pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c0 + i < a.E) sum = __fadd_rn(sum, __uint_as_float(r[i]));
+          }
+          inv = __frcp_rn(sum);
+        }
+        if (split) {
+          if (owner) x_inv[row] = inv;
+          named_bar_sync(pair_bar, 64);
+          if (!owner) inv = x_inv[row];
+        }
+        // pass 3: probabilities and top-k over this thread's chunks
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          tmem_ld16(taddr + c0, r);
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int e = c0 + i;
+            if (e < a.E) {
+              const float p = __fmul_rn(__uint_as_float(r[i]), inv);
+              if (a.probs && valid) a.probs[t * a.E + e] = p;
+              topk_insert<KMAX>(tv, ti, p, e);
+            }
+          }
+        }
+        if (split) {
+          // the helper's list (higher expert ids, descending) is inserted after the owner's:
+          // the merged list equals the sequential insertion over all experts
+          tc_fence_before();
+          if (!owner) {
+  #pragma unroll
+            for (int j = 0; j < KMAX; ++j) {
+              x_tv[j * kBM + row] = tv[j];
+              x_ti[j * kBM + row] = ti[j];
+            }
+          }
+          named_bar_sync(pair_bar, 64);
+          if (owner) {
+  #pragma unroll
+            for (int j = 0; j < KMAX; ++j) topk_insert<KMAX>(tv, ti, x_tv[j * kBM + row], x_ti[j * kBM + row]);
+          }
         }
       }
       if (!owner) continue;
@@ -471,7 +611,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             a.ids[t * a.k + j] = ti[j];
             if (a.weights) a.weights[t * a.k + j] = w;
             if (a.weights_bf16) a.weights_bf16[t * a.k + j] = __float2bfloat16_rn(w);
-            if (a.do_perm) atomicOr(&h->bits[ti[j] * 4 + (row >> 5)], 1u << (row & 31));
+            if (a.do_perm) {
+              atomicOr(&h->bits[ti[j] * 4 + (row >> 5)], 1u << (row & 31));
+              if (one_tile) tile_ids[row * KMAX + j] = ti[j];
+            }
           }
         }
       }
@@ -484,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) {
             b[i] = h->bits[e * 4 + i];
             cnt += __popc(b[i]);
-            h->bits[e * 4 + i] = 0u;
+            if (!one_tile) h->bits[e * 4 + i] = 0u;   // one tile per CTA: kept for the scatter
           }
           a.tile_counts[(int64_t)tile * a.E + e] = cnt;
           uint4 bv = make_uint4(b[0], b[1], b[2], b[3]);
@@ -500,8 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------------------------------------------------------- permutation phase
   if (a.do_perm) {
     if (tid == 0) {
-      __threadfence();
-      atomicAdd(a.grid_sync, 1u);
+      // release: the CTA's counts and bitmaps (ordered before by the barrier above) become
+      // visible with the arrival; acquire on the poll that sees every arrival
+      red_release_gpu_add(a.grid_sync, 1u);
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
       while (ld_acquire_gpu(a.grid_sync) < gridDim.x) {
@@ -511,12 +655,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      __threadfence();
     }
     __syncthreads();
-    if (!*abort_flag)
-      perm_phase<KMAX, kThreads>(a, reinterpret_cast<int32_t*>(base), (int)(((size_t)a.stages * a.stage_bytes) / 4),
-                                 h->total, h->offs);
+    if (!*abort_flag) {
+      if (one_tile)
+        perm_phase_one_tile<KMAX, kThreads>(a, reinterpret_cast<int32_t*>(base), tile_ids, h->bits, h->total,
+                                            h->offs);
+      else
+        perm_phase<KMAX, kThreads>(a, reinterpret_cast<int32_t*>(base), area_ints, h->total, h->offs);
+    }
   }
 
   __syncthreads();
