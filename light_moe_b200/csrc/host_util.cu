@@ -108,6 +108,62 @@ int set_max_dynamic_smem(const void* fn, size_t smem) {
   return LMOE_OK;
 }
 
+namespace {
+// Encoded tensor maps by (address, type, shape, strides, box, swizzle): a layer call encodes
+// the same few maps every time, and a map depends on nothing else, so an entry never goes
+// stale.  Direct-mapped, 256 slots.
+struct TmapKey {
+  const void* base;
+  uint64_t dims[3];
+  uint64_t strides[2];
+  uint32_t box[3];
+  uint32_t dtype, rank, swizzle;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && dtype == o.dtype && rank == o.rank && swizzle == o.swizzle &&
+           dims[0] == o.dims[0] && dims[1] == o.dims[1] && dims[2] == o.dims[2] && strides[0] == o.strides[0] &&
+           strides[1] == o.strides[1] && box[0] == o.box[0] && box[1] == o.box[1] && box[2] == o.box[2];
+  }
+};
+struct TmapSlot {
+  bool used = false;
+  TmapKey key;
+  CUtensorMap map;
+};
+constexpr int kTmapSlots = 256;
+TmapSlot g_tmap[kTmapSlots];
+std::mutex g_tmap_mu;
+
+uint32_t tmap_slot(const TmapKey& k) {
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+  mix(reinterpret_cast<uintptr_t>(k.base));
+  for (int i = 0; i < 3; ++i) mix(k.dims[i]);
+  mix(k.strides[0]);
+  mix(k.strides[1]);
+  for (int i = 0; i < 3; ++i) mix(k.box[i]);
+  mix(k.dtype);
+  mix(k.rank);
+  mix(k.swizzle);
+  return (uint32_t)(h ^ (h >> 32)) % kTmapSlots;
+}
+
+bool tmap_lookup(const TmapKey& k, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  const TmapSlot& e = g_tmap[tmap_slot(k)];
+  if (!e.used || !(e.key == k)) return false;
+  *out = e.map;
+  return true;
+}
+
+void tmap_store(const TmapKey& k, const CUtensorMap& m) {
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  TmapSlot& e = g_tmap[tmap_slot(k)];
+  e.used = true;
+  e.key = k;
+  e.map = m;
+}
+}  // namespace
+
 int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                    uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols,
                    bool swizzle128) {
@@ -124,6 +180,9 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
   if (!aligned16(base) || (row_stride_bytes % 16) != 0) return LMOE_ERR_INVALID_ARG;
   if (box_rows == 0 || box_rows > 256 || box_cols == 0 || box_cols > 256) return LMOE_ERR_INVALID_ARG;
   if (swizzle128 && box_cols * elem_bytes != 128) return LMOE_ERR_INVALID_ARG;
+  const TmapKey key = {base, {cols, rows, 0}, {row_stride_bytes, 0}, {box_cols, box_rows, 0}, (uint32_t)dtype, 2u,
+                       swizzle128 ? 1u : 0u};
+  if (tmap_lookup(key, map)) return LMOE_OK;
   cuuint64_t gdim[2] = {cols, rows};
   cuuint64_t gstride[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
@@ -132,7 +191,9 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_INVALID_ARG;
+  if (r != CUDA_SUCCESS) return LMOE_ERR_INVALID_ARG;
+  tmap_store(key, *map);
+  return LMOE_OK;
 }
 
 int encode_tmap_kblocks(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
@@ -147,6 +208,9 @@ int encode_tmap_kblocks(CUtensorMap* map, const void* base, CUtensorMapDataType 
   const uint64_t blk = 128 / elem_bytes;   // elements per 128-byte block
   if (!aligned16(base) || (row_stride_bytes % 16) != 0 || cols % blk != 0) return LMOE_ERR_INVALID_ARG;
   if (box_rows == 0 || box_rows > 256 || box_blocks == 0 || box_blocks > 256) return LMOE_ERR_INVALID_ARG;
+  const TmapKey key = {base, {blk, rows, cols / blk}, {row_stride_bytes, 128}, {(uint32_t)blk, box_rows, box_blocks},
+                       (uint32_t)dtype, 3u, 1u};
+  if (tmap_lookup(key, map)) return LMOE_OK;
   cuuint64_t gdim[3] = {blk, rows, cols / blk};
   cuuint64_t gstride[2] = {row_stride_bytes, 128};
   cuuint32_t box[3] = {(cuuint32_t)blk, box_rows, box_blocks};
@@ -154,7 +218,9 @@ int encode_tmap_kblocks(CUtensorMap* map, const void* base, CUtensorMapDataType 
   CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), gdim, gstride, box, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_INVALID_ARG;
+  if (r != CUDA_SUCCESS) return LMOE_ERR_INVALID_ARG;
+  tmap_store(key, *map);
+  return LMOE_OK;
 }
 
 }  // namespace lmoe
