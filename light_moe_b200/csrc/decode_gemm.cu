@@ -98,6 +98,8 @@ struct Geo {
   static_assert(kSR >= kQS + kPS, "a scale-ring slot is rewritten only after the epilogue read it");
   static_assert(kTS % kGroups == 0 && kTokLead % kGroups == 0 && kTokLead + kGroups <= kTS,
                 "a token slot is reloaded by the issuer that used it, after its MMAs");
+  static_assert(kTS - kTokLead >= kPS && kTokLead + kPS <= kTS,
+                "the partial-sum check of a stage covers the MMAs of the token slot it reloads");
 };
 
 struct DecodeArgs {
@@ -124,9 +126,7 @@ struct DecodeArgs {
 //     phase): the epilogue waits for
 //     stage it -- stage it + kRing needs the partial-sum slot the epilogue frees after
 //     reading stage it + kRing - kPS > it; the dequantisers wait for stage it - kQS before
-//     reusing its q slot -- stage it - kQS + kRing needs this stage's q first; an issuer
-//     waits for its own stage it - kTS before loading the tokens of stage it into its slot
-//     -- stage it - kTS + kRing = it needs these tokens first;
+//     reusing its q slot -- stage it - kQS + kRing needs this stage's q first;
 //   tok_full[s] (dequantiser warp 0 of the stage's group): the tokens of stage it + kTS
 //     are loaded by the stage's issuer before its MMAs of stage it + kTS - kTokLead, which
 //     come after the MMAs of stage it, which need this wait first;
@@ -337,52 +337,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kGroups && t_on; ++k) t_on = cursor_next(tc, bars, total, a.ksplit, ks_per);
       };
       while (t_on && tc.it < (uint32_t)kTokLead) load_tokens();
-      uint32_t it = 0, p_seen = 0;
-      int e_hint = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const DTile t = dtile_at(bars, tile, e_hint, a.ksplit);
-        const uint32_t n_eff = (uint32_t)((t.rows + 15) & ~15);
+      // walk only this issuer's stages (a single thread here runs its bookkeeping slowly:
+      // no iterations over the other issuers' stages)
+      Cursor c;
+      bool on = cursor_start(c, bars, total, a.ksplit);
+      for (uint32_t k = 0; k < me && on; ++k) on = cursor_next(c, bars, total, a.ksplit, ks_per);
+      uint32_t p_seen = 0;
+      while (on) {
+        const uint32_t it = c.it;
+        const uint32_t n_eff = (uint32_t)((c.t.rows + 15) & ~15);
         const uint32_t idesc = idesc_bf16_f32(kBM, n_eff);
-        const uint32_t kb_bytes = (t.rows <= 16 ? 16u : 32u) * 128u;   // k-block stride of the token box
-        for (int ks = 0; ks < ks_per; ++ks, ++it) {
-          if (it % kGroups != me) continue;
-          // tokens of stage it + kTokLead: its slot held stage it + kTokLead - kTS <= it - kGroups,
-          // this issuer's own earlier stage, whose MMAs must be done
-          if (t_on && tc.it == it + kTokLead) {
-            const uint32_t j = tc.it - kTS;
-            if (tc.it >= (uint32_t)kTS &&
-                !mbar_wait(&bars->stage_done[j % kRing], (j / kRing) & 1u, a.err, abort_flag, kSite + 7)) {
-              ok = false;
-              break;
-            }
-            load_tokens();
-          }
-          // q of stage it in tensor memory (all four warps of the group) and its tokens
-          // landed; the partial-sum slot's previous stage it - kPS read by the epilogue
-          bool ready = counter4_wait(bars->q_ready[me], it, nullptr, a.err, abort_flag, kSite + 5);
-          if (ready && it >= (uint32_t)G::kPS && p_seen <= it - G::kPS)
-            ready = counter4_wait(bars->p_rel, it - G::kPS, &p_seen, a.err, abort_flag, kSite + 6);
-          if (!ready) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem + G::kTmemP + (it % G::kPS) * G::kPCols;
-          const uint32_t a_tmem = tmem + (it % G::kQS) * 64;
-          const uint32_t bsm = smem_u32(b_stages + (it % kTS) * kBStageBytes);
+        const uint32_t kb_bytes = (c.t.rows <= 16 ? 16u : 32u) * 128u;   // k-block stride of the token box
+        // q of stage it in tensor memory (all four warps of the group) and its tokens
+        // landed; the partial-sum slot's previous stage it - kPS read by the epilogue
+        bool ready = counter4_wait(bars->q_ready[me], it, nullptr, a.err, abort_flag, kSite + 5);
+        if (ready && it >= (uint32_t)G::kPS && p_seen <= it - G::kPS)
+          ready = counter4_wait(bars->p_rel, it - G::kPS, &p_seen, a.err, abort_flag, kSite + 6);
+        if (!ready) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + G::kTmemP + (it % G::kPS) * G::kPCols;
+        const uint32_t a_tmem = tmem + (it % G::kQS) * 64;
+        const uint32_t bsm = smem_u32(b_stages + (it % kTS) * kBStageBytes);
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb) {
-            const uint64_t bdesc = sdesc_k_sw128(bsm + kb * kb_bytes);
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint64_t bdesc = sdesc_k_sw128(bsm + kb * kb_bytes);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {   // +32 bytes along K = +2 in the descriptor's address field
-              const uint32_t accum = SG == 2 ? (kk > 0 ? 1u : 0u) : ((kb | kk) != 0 ? 1u : 0u);
-              mma_ts(d_tmem + (SG == 2 ? (uint32_t)kb * kBN : 0u), a_tmem + kb * 32 + kk * 8,
-                     bdesc + (uint64_t)(2 * kk), idesc, accum);
-            }
+          for (int kk = 0; kk < 4; ++kk) {   // +32 bytes along K = +2 in the descriptor's address field
+            const uint32_t accum = SG == 2 ? (kk > 0 ? 1u : 0u) : ((kb | kk) != 0 ? 1u : 0u);
+            mma_ts(d_tmem + (SG == 2 ? (uint32_t)kb * kBN : 0u), a_tmem + kb * 32 + kk * 8,
+                   bdesc + (uint64_t)(2 * kk), idesc, accum);
           }
-          mma_commit(&bars->stage_done[it % kRing]);   // frees q / tokens, publishes the partial sums
         }
+        mma_commit(&bars->stage_done[it % kRing]);   // frees q / tokens, publishes the partial sums
+        // tokens of stage it + kTokLead: its slot held stage it + kTokLead - kTS, whose partial
+        // sums the epilogue has read (p_seen > it - kPS >= it + kTokLead - kTS), so its MMAs
+        // are done; before kPS stages the slot has not been used yet
+        if (t_on && tc.it == it + kTokLead) load_tokens();
+        for (int k = 0; k < kGroups && on; ++k) on = cursor_next(c, bars, total, a.ksplit, ks_per);
       }
       mma_commit(&bars->done[me]);
       mbar_wait(&bars->done[me], 0, a.err, nullptr, kSite + 8);
