@@ -11,7 +11,7 @@
 // decode-sized batch (a handful of tokens per expert) still fills the 128-row MMA; the
 // accumulator tile is [128 weight rows x BN tokens] in tensor memory.
 //
-// W4A16 weights (the north-star path): one prepacked int4 super-block (128 rows x 128 K,
+// W4A16 weights (the MoE-layer hot path): one prepacked int4 super-block (128 rows x 128 K,
 // scales embedded, w4_layout.cuh) per pipeline stage arrives by one bulk copy; dequantiser
 // warps turn it into bf16 and write it with tcgen05.st straight into tensor memory, where
 // tcgen05.mma reads it as the A operand ("TS" form); the token tile (B operand) arrives by
