@@ -239,9 +239,14 @@ def extra_workloads(ex, stream, peaks, peak_kind, device):
 
     out = {}
     g = torch.Generator(device=device).manual_seed(0)
-    # router: x [16384, 4096] bf16, W [E, 4096]; HBM-bound on the x stream
+    # router: x [16384, 4096] bf16, W [E, 4096]; HBM-bound on the x stream.  Right after the
+    # GEMM-heavy measurements the GPU runs memory-bound kernels ~15 % slower for a few seconds
+    # (the router alone: 35 us after an idle pause, 41 us straight after 20 prefill layers), so
+    # the router is timed after a 3 s pause, like a kernel timed on its own
     T = 16384
     x = torch.randn(T, D, generator=g, device=device).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    time.sleep(3.0)
     router = []
     for e, k in ((8, 2), (64, 6)):
         w = (torch.randn(e, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
@@ -252,7 +257,7 @@ def extra_workloads(ex, stream, peaks, peak_kind, device):
         gbs = nbytes / secs / 1e9
         router.append({"experts": e, "top_k": k, "tokens": T, "us": round(secs * 1e6, 1), "GB/s": round(gbs, 1),
                        "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes": nbytes,
-                       "timing": "CUDA graph of 20 calls", "eager_us": round(eager * 1e6, 1)})
+                       "timing": "CUDA graph of 20 calls, after a 3 s idle pause", "eager_us": round(eager * 1e6, 1)})
     out["router"] = router
     del x
     # grouped GEMMs (gate/up + SwiGLU, down) over 8192 rows, Zipf(1.2) expert load
@@ -389,6 +394,11 @@ def measure_decode(args, x, gw, ex, layer, ws, stream, barrier, peaks, peak_kind
 
     from light_moe_b200.layer import W4A16MoELayer
     xd = x[:T_DECODE].contiguous()
+    # a decode loop is memory-bound and runs at a lower power level than the prefill GEMMs
+    # timed just before; memory-bound kernels run ~15 % slower for a few seconds after those,
+    # so the decode step is timed after a 3 s pause
+    torch.cuda.synchronize()
+    time.sleep(3.0)
     check = None
     if ws > 1:
         from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
@@ -415,7 +425,7 @@ def measure_decode(args, x, gw, ex, layer, ws, stream, barrier, peaks, peak_kind
     layer_gbs = wbytes / graph / 1e9
     out = {"tokens_per_gpu": T_DECODE, "value": round(T_DECODE * ws / graph, 1), "unit": "tokens/s",
            "ms_per_step": round(graph * 1e3, 4), "eager_ms_per_step": round(eager * 1e3, 4),
-           "timing": "CUDA graph replay of 10 steps (max over ranks); eager: back-to-back calls",
+           "timing": "CUDA graph replay of 10 steps (max over ranks), after a 3 s idle pause; eager: back-to-back calls",
            "dispatch": "fixed-capacity all-to-all, no host synchronisation" if ws > 1 else "single GPU",
            "layer_weight_stream_gbs_per_gpu": round(layer_gbs, 1),
            "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4)}
