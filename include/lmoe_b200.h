@@ -233,6 +233,29 @@ int lmoe_w4a16_grouped_gemm(const void* input, int64_t total_rows, int K, const 
  * Replaces unpermute_tokens (python/light_moe/ops/grouped_gemm.py:250-279) and the
  * expert-parallel unsort + weighted sum (python/light_moe/distributed/expert_parallel.py:
  * 307-317). */
+/* Fixed-capacity expert-parallel exchange (decode): every rank sends every rank a block of
+ * capacity_rows = capacity_tokens * top_k rows, so the all-to-alls have equal splits and no
+ * count reaches the host.  All arrays are device int32.
+ * Send plan: counts [ep * experts_per_rank] rows of this rank per (destination rank, local
+ * expert) in router order; sorted_idx / positions the router's order and its inverse
+ * [num_tokens * top_k]. Writes send_index [ep * capacity_rows] (the sorted row carried by each
+ * slot of each destination's block, 0 for padding: gather rows with lmoe_permute_rows) and
+ * combine_pos [num_tokens * top_k] (the slot, in the returned blocks, of each (token, choice):
+ * the positions argument of lmoe_combine_rows). num_tokens * top_k <= capacity_rows.
+ * Receive plan: recv_counts [ep * experts_per_rank] rows received per (source rank, local
+ * expert). Writes regroup [ep * capacity_rows] (received row at each expert-major position:
+ * expert 0 from every source, expert 1, ..., then all padding), restore (its inverse) and
+ * seg_offsets [experts_per_rank + num_shared + 2] (the local experts' segments, one padding
+ * hole for segment map entry -1, then num_shared segments of num_tokens rows).
+ * New: the reference pads to equal splits by sending every token to every rank
+ * (python/light_moe/distributed/expert_parallel.py:186-244). */
+int lmoe_capacity_send_plan(const int32_t* counts, const int32_t* sorted_idx, const int32_t* positions,
+                            int64_t num_tokens, int top_k, int ep, int experts_per_rank, int64_t capacity_rows,
+                            int32_t* send_index, int32_t* combine_pos, lmoe_stream_t stream);
+int lmoe_capacity_receive_plan(const int32_t* recv_counts, int ep, int experts_per_rank, int64_t capacity_rows,
+                               int num_shared, int64_t num_tokens, int32_t* regroup, int32_t* restore,
+                               int32_t* seg_offsets, lmoe_stream_t stream);
+
 int lmoe_combine_rows(const void* rows, const int32_t* positions, const float* weights,
                       int64_t num_tokens, int top_k, int hidden_size,
                       const void* extra_rows, int num_extra, void* y, lmoe_stream_t stream);

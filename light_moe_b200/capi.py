@@ -34,6 +34,8 @@ SIGNATURES = {
     "lmoe_status_string": (ctypes.c_char_p, [_I]),
     "lmoe_read_error": (_I, [_P, _P, _P]),
     "lmoe_set_gemm_sm_limit": (_I, [_I]),
+    "lmoe_capacity_send_plan": (_I, [_P, _P, _P, _I64, _I, _I, _I, _I64, _P, _P, _P]),
+    "lmoe_capacity_receive_plan": (_I, [_P, _I, _I, _I64, _I, _I64, _P, _P, _P, _P]),
     "lmoe_get_gemm_sm_limit": (_I, []),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),

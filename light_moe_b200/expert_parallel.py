@@ -165,6 +165,24 @@ class CudaExpertBackend:
                   rows.shape[1], 1, out.data_ptr(), capi.stream_handle())
         return out
 
+    def capacity_send_plan(self, counts, sidx, pos, T, k, ep, epr, C):
+        from . import capi
+        send_index = torch.empty(ep * C, dtype=torch.int32, device=counts.device)
+        combine_pos = torch.empty(T * k, dtype=torch.int32, device=counts.device)
+        capi.call("lmoe_capacity_send_plan", counts.data_ptr(), sidx.data_ptr(), pos.data_ptr(), T, k, ep, epr, C,
+                  send_index.data_ptr(), combine_pos.data_ptr(), capi.stream_handle())
+        return send_index, combine_pos
+
+    def capacity_receive_plan(self, recv_counts, ep, epr, C, S, T):
+        from . import capi
+        dev = recv_counts.device
+        regroup = torch.empty(ep * C, dtype=torch.int32, device=dev)
+        restore = torch.empty(ep * C, dtype=torch.int32, device=dev)
+        seg_offsets = torch.empty(epr + S + 2, dtype=torch.int32, device=dev)
+        capi.call("lmoe_capacity_receive_plan", recv_counts.data_ptr(), ep, epr, C, S, T, regroup.data_ptr(),
+                  restore.data_ptr(), seg_offsets.data_ptr(), capi.stream_handle())
+        return regroup, restore, seg_offsets
+
     def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         if self.sm_limit is None:
             return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows)
@@ -268,22 +286,12 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             raise ValueError(f"{T} tokens exceed capacity_tokens={self.capacity_tokens}")
         C = self.capacity_tokens * k                  # rows per destination block
         dev = x.device
-        self.kernels_per_step = 5
+        self.kernels_per_step = 9
         if T > 0:
             ids, w, counts, offsets, sidx, pos = be.route(x, self.gate_weight, self.gate_bias)
             counts = counts.view(ep, epr).to(torch.int32)
-            # sorted row j (destination-rank order) -> padded send row r(j) * C + j - start[r(j)]
-            cnt_r = counts.sum(1)
-            end_r = torch.cumsum(cnt_r, 0)
-            start_r = end_r - cnt_r
-            j = torch.arange(T * k, device=dev, dtype=end_r.dtype)
-            r_of_j = torch.searchsorted(end_r, j, right=True)
-            p = r_of_j * C + (j - start_r[r_of_j])
-            # padded send block: slot r * C + c holds sorted row start[r] + c (padding: row 0)
-            c = torch.arange(C, device=dev, dtype=end_r.dtype)
-            src = (start_r[:, None] + c[None, :]).clamp(max=T * k - 1)
-            padded_sidx = torch.where(c[None, :] < cnt_r[:, None], sidx.long()[src], torch.zeros_like(src))
-            send = be.gather(x, padded_sidx.to(torch.int32).flatten())
+            send_index, combine_pos = be.capacity_send_plan(counts, sidx, pos, T, k, ep, epr, C)
+            send = be.gather(x, send_index)
         else:
             counts = torch.zeros(ep, epr, dtype=torch.int32, device=dev)
             send = torch.zeros(ep * C, d, dtype=x.dtype, device=dev)
@@ -292,39 +300,22 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         g.all_to_all(recv_counts, counts.contiguous())
         recv = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
         g.all_to_all(recv, send)
-        # regroup the received rows expert-major (each local expert one segment, so its
-        # weights stream once whatever the number of source ranks): g[j] = the received row
-        # at expert-major position j; every source's padding becomes one trailing hole, so
-        # g is a permutation of the ep * C rows and its inverse is a scatter
-        rc = recv_counts.long()
-        cnt = torch.cat([rc, C - rc.sum(1, keepdim=True)], 1)                        # [ep, epr + 1]
-        src_start = (torch.arange(ep, device=dev) * C)[:, None] + torch.cumsum(cnt, 1) - cnt
-        cnt_em = cnt.t().contiguous().flatten()                                       # (expert, source)
-        dst_start = torch.cumsum(cnt_em, 0) - cnt_em
-        jj = torch.arange(ep * C, device=dev)
-        kk = torch.searchsorted(dst_start, jj, right=True) - 1
-        g_idx = src_start.t().contiguous().flatten()[kk] + (jj - dst_start[kk])
-        inv = torch.empty_like(g_idx)
-        inv[g_idx] = jj
+        # regroup the received rows expert-major (each local expert one segment, so its weights
+        # stream once whatever the number of source ranks); every source's padding becomes one
+        # trailing hole
+        regroup, restore, seg_offsets = be.capacity_receive_plan(recv_counts, ep, epr, C, S, T)
         rows_em = torch.empty(ep * C + S * T, d, dtype=x.dtype, device=dev)
-        rows_em[: ep * C] = be.take(recv, g_idx.to(torch.int32))
+        rows_em[: ep * C] = be.take(recv, regroup)
         for s in range(S):
             rows_em[ep * C + s * T: ep * C + (s + 1) * T].copy_(x)
-        # segments: the local experts, the padding hole, the shared experts on local tokens
-        seg_counts = cnt_em.view(epr + 1, ep).sum(1)
-        if S:
-            seg_counts = torch.cat([seg_counts, torch.full((S,), T, dtype=torch.long, device=dev)])
-        seg_offsets = torch.cat([torch.zeros(1, dtype=torch.long, device=dev),
-                                 torch.cumsum(seg_counts, 0)]).to(torch.int32)
-        out_em = be.experts(rows_em, seg_offsets, self._capacity_segments(dev), seg_counts.numel(),
-                            self.capacity_tokens)
-        out = be.take(out_em, inv.to(torch.int32))                                     # back to capacity order
+        out_em = be.experts(rows_em, seg_offsets, self._capacity_segments(dev), epr + 1 + S, self.capacity_tokens)
+        out = be.take(out_em, restore)                                              # back to capacity order
         ret = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
         g.all_to_all(ret, out)
         extra = out_em[ep * C:] if S else None
         if T == 0:
             return torch.empty(0, d, dtype=x.dtype, device=dev)
-        return be.combine(ret, p[pos.long()].to(torch.int32), w, T, extra, S)
+        return be.combine(ret, combine_pos, w, T, extra, S)
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         x = hidden_states.reshape(-1, hidden_states.shape[-1])
@@ -390,6 +381,43 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             ys.append(be.combine(mb["ret"], mb["pos"], mb["w"], mb["T"], extra, S))
         y = ys[0] if nmb == 1 else torch.cat(ys)
         return y.view(hidden_states.shape)
+
+
+def capacity_send_plan_torch(counts, sidx, pos, T: int, k: int, ep: int, epr: int, C: int):
+    """The fixed-capacity send plan (lmoe_capacity_send_plan) in torch index operations:
+    (send_index [ep * C], combine_pos [T * k]), int32 on counts' device."""
+    dev = counts.device
+    cnt_r = counts.view(ep, epr).to(torch.int64).sum(1)
+    end_r = torch.cumsum(cnt_r, 0)
+    start_r = end_r - cnt_r
+    j = torch.arange(T * k, device=dev, dtype=torch.int64)
+    r_of_j = torch.searchsorted(end_r, j, right=True)
+    p = r_of_j * C + (j - start_r[r_of_j])          # sorted row -> slot of its destination's block
+    c = torch.arange(C, device=dev, dtype=torch.int64)
+    src = (start_r[:, None] + c[None, :]).clamp(max=max(T * k - 1, 0))
+    send_index = torch.where(c[None, :] < cnt_r[:, None], sidx.long()[src], torch.zeros_like(src))
+    return send_index.to(torch.int32).flatten(), p[pos.long()].to(torch.int32)
+
+
+def capacity_receive_plan_torch(recv_counts, ep: int, epr: int, C: int, S: int, T: int):
+    """The fixed-capacity receive plan (lmoe_capacity_receive_plan) in torch index operations:
+    (regroup [ep * C], restore [ep * C], seg_offsets [epr + S + 2]), int32."""
+    dev = recv_counts.device
+    rc = recv_counts.view(ep, epr).long()
+    cnt = torch.cat([rc, C - rc.sum(1, keepdim=True)], 1)                        # [ep, epr + 1]
+    src_start = (torch.arange(ep, device=dev) * C)[:, None] + torch.cumsum(cnt, 1) - cnt
+    cnt_em = cnt.t().contiguous().flatten()                                       # (expert, source)
+    dst_start = torch.cumsum(cnt_em, 0) - cnt_em
+    jj = torch.arange(ep * C, device=dev)
+    kk = torch.searchsorted(dst_start, jj, right=True) - 1
+    regroup = src_start.t().contiguous().flatten()[kk] + (jj - dst_start[kk])
+    restore = torch.empty_like(regroup)
+    restore[regroup] = jj
+    seg_counts = cnt_em.view(epr + 1, ep).sum(1)
+    if S:
+        seg_counts = torch.cat([seg_counts, torch.full((S,), T, dtype=torch.long, device=dev)])
+    seg_offsets = torch.cat([torch.zeros(1, dtype=torch.long, device=dev), torch.cumsum(seg_counts, 0)])
+    return regroup.to(torch.int32), restore.to(torch.int32), seg_offsets.to(torch.int32)
 
 
 def slice_experts(ex: W4A16Experts, e0: int, e1: int) -> W4A16Experts:

@@ -31,6 +31,14 @@ class OracleExpertBackend:
     def gather(self, x, sorted_idx):
         return x[(sorted_idx // self.top_k).long()].contiguous()
 
+    def capacity_send_plan(self, counts, sidx, pos, T, k, ep, epr, C):
+        from light_moe_b200.expert_parallel import capacity_send_plan_torch
+        return capacity_send_plan_torch(counts, sidx, pos, T, k, ep, epr, C)
+
+    def capacity_receive_plan(self, recv_counts, ep, epr, C, S, T):
+        from light_moe_b200.expert_parallel import capacity_receive_plan_torch
+        return capacity_receive_plan_torch(recv_counts, ep, epr, C, S, T)
+
     def take(self, rows, index):
         return rows[index.long()].contiguous()
 
