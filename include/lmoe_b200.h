@@ -256,6 +256,48 @@ int lmoe_capacity_receive_plan(const int32_t* recv_counts, int ep, int experts_p
                                int num_shared, int64_t num_tokens, int32_t* regroup, int32_t* restore,
                                int32_t* seg_offsets, lmoe_stream_t stream);
 
+/* Expert-parallel exchange over peer memory (NVLink), replacing the NCCL all-to-alls of    */
+/* python/light_moe/distributed/expert_parallel.py:186-244 and :275-319.  Every rank         */
+/* allocates one buffer of lmoe_p2p_buffer_bytes (same geometry on all ranks; Tc = the      */
+/* capacity_tokens every rank passes, num_tokens <= Tc per step) with lmoe_p2p_alloc, sends  */
+/* the 64-byte IPC handle to the others, maps theirs with lmoe_p2p_open and keeps a device   */
+/* array peers[ep] of the mapped bases (its own allocation at peers[me]).  One step:          */
+/*   lmoe_p2p_exchange_counts  counts[E] (the router's) -> seg_offsets[E/ep + 2 + S], the     */
+/*                             local segments (experts, a hole, S shared segments of T rows)  */
+/*                             of the rows region, and dst_base[E] (scratch for dispatch)     */
+/*   lmoe_p2p_dispatch         x rows in router order straight into the owners' rows regions */
+/*   lmoe_p2p_wait(which = 1)  the rows of every peer arrived: run the grouped GEMMs on the   */
+/*                             rows region (at rows_offset; segment e's weight: experts        */
+/*                             0..E/ep-1, -1 for the hole, then the shared experts)           */
+/*   lmoe_p2p_send_back        the down GEMM's routed output rows back to their sources' ret  */
+/*                             regions (slot t*k + j)                                         */
+/*   lmoe_p2p_wait(which = 2)  every routed output of this rank's tokens is in its ret region */
+/*                             (at ret_offset): lmoe_combine_rows with positions = slot       */
+/* state: int32[4] on the device, zeroed once ([0] step epoch, [1] error word: nonzero when a  */
+/* wait ran out of time or counts were inconsistent, [2], [3] internal counters).  Waits are  */
+/* bounded (2 s); every rank must run every step, in the same order.                          */
+size_t lmoe_p2p_buffer_bytes(int ep, int num_experts, int64_t capacity_tokens, int top_k, int num_shared,
+                             int hidden);
+int lmoe_p2p_buffer_offsets(int ep, int num_experts, int64_t capacity_tokens, int top_k, int num_shared,
+                            int hidden, size_t* rows_offset, size_t* ret_offset);
+int lmoe_p2p_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int lmoe_p2p_open(const void* ipc_handle, void** ptr);
+int lmoe_p2p_close(void* ptr);
+int lmoe_p2p_free(void* ptr);
+int lmoe_p2p_exchange_counts(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens,
+                             int top_k, int num_shared, int hidden, int64_t num_tokens, int32_t* state,
+                             const int32_t* counts, int32_t* seg_offsets, int32_t* dst_base,
+                             lmoe_stream_t stream);
+int lmoe_p2p_dispatch(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
+                      int num_shared, int hidden, int64_t num_tokens, int32_t* state, const void* x,
+                      const int32_t* sorted_idx, const int32_t* ids, const int32_t* offsets,
+                      const int32_t* dst_base, lmoe_stream_t stream);
+int lmoe_p2p_wait(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
+                  int num_shared, int hidden, int64_t num_tokens, int32_t* state, int which, lmoe_stream_t stream);
+int lmoe_p2p_send_back(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
+                       int num_shared, int hidden, int64_t num_tokens, int32_t* state, const void* out,
+                       const int32_t* seg_offsets, lmoe_stream_t stream);
+
 int lmoe_combine_rows(const void* rows, const int32_t* positions, const float* weights,
                       int64_t num_tokens, int top_k, int hidden_size,
                       const void* extra_rows, int num_extra, void* y, lmoe_stream_t stream);

@@ -29,7 +29,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 CU_SOURCES = ["host_util.cu", "router.cu", "quant.cu", "grouped_gemm.cu", "decode_gemm.cu", "simt_gemm.cu",
-              "layer.cu", "dispatch.cu"]
+              "layer.cu", "dispatch.cu", "ep_p2p.cu"]
 HEADERS = ["ptx.cuh", "lmoe_math.cuh", "host_util.h", "w4_layout.cuh", "w4_dequant.cuh", "grouped_gemm.h",
            "decode_gemm.h"]
 NVCC_FLAGS = [

@@ -36,6 +36,16 @@ SIGNATURES = {
     "lmoe_set_gemm_sm_limit": (_I, [_I]),
     "lmoe_capacity_send_plan": (_I, [_P, _P, _P, _I64, _I, _I, _I, _I64, _P, _P, _P]),
     "lmoe_capacity_receive_plan": (_I, [_P, _I, _I, _I64, _I, _I64, _P, _P, _P, _P]),
+    "lmoe_p2p_buffer_bytes": (_SZ, [_I, _I, _I64, _I, _I, _I]),
+    "lmoe_p2p_buffer_offsets": (_I, [_I, _I, _I64, _I, _I, _I, _P, _P]),
+    "lmoe_p2p_alloc": (_I, [_SZ, _P, _P]),
+    "lmoe_p2p_open": (_I, [_P, _P]),
+    "lmoe_p2p_close": (_I, [_P]),
+    "lmoe_p2p_free": (_I, [_P]),
+    "lmoe_p2p_exchange_counts": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _P, _P]),
+    "lmoe_p2p_dispatch": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P]),
+    "lmoe_p2p_wait": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _I, _P]),
+    "lmoe_p2p_send_back": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _P]),
     "lmoe_get_gemm_sm_limit": (_I, []),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),

@@ -219,10 +219,10 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
                  backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1,
                  dispatch: str = "exact", capacity_tokens: Optional[int] = None, sm_reserve: Optional[int] = None):
         super().__init__()
-        if dispatch not in ("exact", "capacity"):
-            raise ValueError(f"dispatch must be 'exact' or 'capacity', not {dispatch!r}")
-        if dispatch == "capacity" and (capacity_tokens is None or int(capacity_tokens) < 1):
-            raise ValueError("capacity dispatch needs capacity_tokens >= 1 (the same on every rank)")
+        if dispatch not in ("exact", "capacity", "p2p"):
+            raise ValueError(f"dispatch must be 'exact', 'capacity' or 'p2p', not {dispatch!r}")
+        if dispatch in ("capacity", "p2p") and (capacity_tokens is None or int(capacity_tokens) < 1):
+            raise ValueError(f"{dispatch} dispatch needs capacity_tokens >= 1 (the same on every rank)")
         self.dispatch = dispatch
         self.capacity_tokens = int(capacity_tokens) if capacity_tokens is not None else None
         self.config = config
@@ -244,6 +244,16 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         # micro-batch (set by the last forward)
         self.kernels_per_step = 5
         self._seg_cache = {}
+        # dispatch="p2p": rows move through peer memory (collective setup of the symmetric
+        # buffers here, outside any CUDA graph capture)
+        self.exchange = None
+        if dispatch == "p2p":
+            if not isinstance(backend, CudaExpertBackend):
+                raise ValueError("p2p dispatch runs on the CUDA expert backend only")
+            from .peer_exchange import PeerExchange
+            self.exchange = PeerExchange(ep_group, config.num_experts, self.capacity_tokens, config.top_k,
+                                         config.num_shared, config.hidden_size,
+                                         torch.device("cuda", torch.cuda.current_device()))
 
     @classmethod
     def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
@@ -317,10 +327,48 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             return torch.empty(0, d, dtype=x.dtype, device=dev)
         return be.combine(ret, combine_pos, w, T, extra, S)
 
+    def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        """Dispatch and return through peer memory: counts exchange, fused permute + send,
+        the local grouped GEMMs on the rows region, fused send-back, weighted combine."""
+        T, d = x.shape
+        cfg, be, px = self.config, self.backend, self.exchange
+        epr, k, S = self.experts_per_rank, cfg.top_k, cfg.num_shared
+        if T > self.capacity_tokens:
+            raise ValueError(f"{T} tokens exceed capacity_tokens={self.capacity_tokens}")
+        dev = x.device
+        self.kernels_per_step = 8
+        x = x.contiguous()
+        if T > 0:
+            ids, w, counts, offsets, sidx, pos = be.route(x, self.gate_weight, self.gate_bias)
+        else:
+            counts = torch.zeros(cfg.num_experts, dtype=torch.int32, device=dev)
+            ids = w = offsets = sidx = None
+        px.exchange_counts(counts, T)
+        px.dispatch(x, sidx, ids, offsets)
+        px.wait_rows(T)
+        out = be.experts(px.rows, px.seg_offsets, self._capacity_segments(dev), epr + 1 + S, self.capacity_tokens)
+        px.send_back(out, T)
+        px.wait_returns(T)
+        if T == 0:
+            return torch.empty(0, d, dtype=x.dtype, device=dev)
+        key = ("slots", T * k, str(dev))
+        if key not in self._seg_cache:
+            self._seg_cache[key] = torch.arange(T * k, dtype=torch.int32, device=dev)
+        extra = out[px.routed_rows: px.routed_rows + S * T] if S else None
+        return be.combine(px.ret[: T * k], self._seg_cache[key], w, T, extra, S)
+
+    def close(self):
+        """Release the peer-exchange buffers (collective; p2p dispatch only)."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         x = hidden_states.reshape(-1, hidden_states.shape[-1])
         if self.dispatch == "capacity":
             return self._forward_capacity(x).view(hidden_states.shape)
+        if self.dispatch == "p2p":
+            return self._forward_p2p(x).view(hidden_states.shape)
         T, d = x.shape
         cfg, g, be = self.config, self.ep_group, self.backend
         ep, epr, k, S = g.ep_size, self.experts_per_rank, cfg.top_k, cfg.num_shared

@@ -1,8 +1,9 @@
 """Expert-parallel layer on GPUs (NCCL): each rank's output must match the single-GPU layer
 on the same tokens with the full expert set (max relative error 1e-2, the layer bar).
 Runs with world size 1 on any box, and with world size 2 when two GPUs are visible.
-The fixed-capacity dispatch (no host copy of the counts) is also captured in a CUDA graph
-and replayed: the replay must reproduce the eager output bit for bit."""
+The fixed-capacity dispatch and the peer-memory dispatch (no host copy of the counts) are
+also captured in a CUDA graph and replayed: the replay must reproduce the eager output bit
+for bit."""
 import os
 import socket
 import sys
@@ -53,8 +54,8 @@ def _worker(rank, world, port, case, q):
         y_ref = ref_layer(x)
         torch.cuda.synchronize()
         err = ((y.float() - y_ref.float()).abs().max() / y_ref.float().abs().max()).item()
-        if case.get("dispatch") == "capacity":
-            # the whole step (router, gather, three all-to-alls, GEMMs, combine) in one graph
+        if case.get("dispatch") in ("capacity", "p2p"):
+            # the whole step (router, gather / peer copies, exchanges, GEMMs, combine) in one graph
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(side):
@@ -68,6 +69,11 @@ def _worker(rank, world, port, case, q):
             if not torch.equal(y_graph, y):
                 err = float("inf")
             del graph, y_graph
+        if case.get("dispatch") == "p2p":
+            torch.cuda.synchronize()
+            if ep_layer.exchange.error() != 0:
+                err = float("inf")
+            ep_layer.close()
         q.put((rank, "ok", err))
         dist.barrier()
         dist.destroy_process_group()
@@ -102,7 +108,12 @@ CASES = [dict(E=8, S=0, k=2, d=512, F=256, g=128, T=[300, 77]),
          dict(E=16, S=0, k=4, d=256, F=128, g=64, T=[333, 150], mb=3),
          # fixed-capacity dispatch: Mixtral decode shape, and shared experts with ragged tokens
          dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64], dispatch="capacity", cap=64),
-         dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="capacity", cap=40)]
+         dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="capacity", cap=40),
+         # rows through peer memory: Mixtral decode shape, shared experts with ragged tokens,
+         # and prefill-sized steps (grouped GEMM tiles)
+         dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64], dispatch="p2p", cap=64),
+         dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="p2p", cap=40),
+         dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[300, 77], dispatch="p2p", cap=300)]
 
 
 @pytest.mark.parametrize("case", CASES)
