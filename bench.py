@@ -402,7 +402,8 @@ def measure_decode(args, x, gw, ex, layer, ws, stream, barrier, peaks, peak_kind
     check = None
     if ws > 1:
         from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
-        dlayer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, dispatch="capacity",
+        dmode = "p2p" if args.ep_dispatch == "p2p" else "capacity"
+        dlayer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, dispatch=dmode,
                                                     capacity_tokens=T_DECODE)
         y_ep = dlayer(xd)
         y_one = W4A16MoELayer(gw, ex, TOPK)(xd)
@@ -426,11 +427,14 @@ def measure_decode(args, x, gw, ex, layer, ws, stream, barrier, peaks, peak_kind
     out = {"tokens_per_gpu": T_DECODE, "value": round(T_DECODE * ws / graph, 1), "unit": "tokens/s",
            "ms_per_step": round(graph * 1e3, 4), "eager_ms_per_step": round(eager * 1e3, 4),
            "timing": "CUDA graph replay of 10 steps (max over ranks), after a 3 s idle pause; eager: back-to-back calls",
-           "dispatch": "fixed-capacity all-to-all, no host synchronisation" if ws > 1 else "single GPU",
+           "dispatch": ("single GPU" if ws == 1 else
+                        "peer-memory copies (NVLink), no NCCL and no host synchronisation" if args.ep_dispatch == "p2p"
+                        else "fixed-capacity NCCL all-to-all, no host synchronisation"),
            "layer_weight_stream_gbs_per_gpu": round(layer_gbs, 1),
            "layer_frac_of_hbm": round(layer_gbs / peaks["hbm_gbs"], 4)}
     if ws > 1:
         out["ep_max_rel_err"] = check
+        dlayer.close()
     else:
         out["roofline_gate_up"] = gemm_roofline(xd, gw, ex, T_DECODE, stream, peaks, peak_kind)
     return out
@@ -458,10 +462,15 @@ def run_ours(args):
     x, gw, ex = make_problem(T, device, seed=0)
     if ws > 1:
         from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
-        layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, micro_batches=args.micro_batches,
-                                                   sm_reserve=args.sm_reserve)
+        if args.ep_dispatch == "p2p":
+            layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, dispatch="p2p", capacity_tokens=T)
+            # router, counts exchange, dispatch, wait, gate/up GEMM, down GEMM, send-back, wait, combine
+            launches_per_step = 9
+        else:
+            layer = ExpertParallelW4A16Layer.from_full(gw, ex, TOPK, group=None, micro_batches=args.micro_batches,
+                                                       sm_reserve=args.sm_reserve)
+            launches_per_step = 5 * layer.micro_batches
         fwd = layer.forward
-        launches_per_step = 5 * layer.micro_batches
     else:
         layer = W4A16MoELayer(gw, ex, TOPK)
         fwd = layer.forward
@@ -555,7 +564,9 @@ def run_ours(args):
             "config": {"workload": "Mixtral-8x7B-shaped W4A16 MoE layer, prefill", "tokens_per_gpu": T,
                        "hidden": D, "ffn": FFN, "experts": E, "top_k": TOPK, "group_size": GROUP,
                        "parallelism": f"ep{ws}" if ws > 1 else "single GPU",
-                       "ep_micro_batches": args.micro_batches if ws > 1 else None,
+                       "ep_dispatch": (None if ws == 1 else "peer-memory copies over NVLink (no NCCL on the data path)"
+                                       if args.ep_dispatch == "p2p" else "NCCL all-to-all-v"),
+                       "ep_micro_batches": args.micro_batches if ws > 1 and args.ep_dispatch != "p2p" else None,
                        "ep_sm_reserve": layer.sm_reserve if ws > 1 else None,
                        "l2": l2_note(ex, ws, T)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
@@ -573,6 +584,8 @@ def run_ours(args):
         }
         print(json.dumps(result), flush=True)
     if ws > 1:
+        if hasattr(layer, "close"):
+            layer.close()
         dist.barrier()
         dist.destroy_process_group()
     return result
@@ -672,6 +685,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the router / skewed-GEMM / fine-grained measurements")
+    ap.add_argument("--ep-dispatch", choices=["p2p", "exact"], default="p2p",
+                    help="N > 1: rows through peer memory (default) or NCCL all-to-alls (exact prefill, "
+                         "fixed-capacity decode)")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="expert-parallel runs: micro-batches whose all-to-alls overlap the GEMMs")
     ap.add_argument("--sm-reserve", type=int, default=None,

@@ -204,7 +204,10 @@ class CudaExpertBackend:
         if self.gemm_timer is not None:
             ev1 = torch.cuda.Event(enable_timing=True)
             ev1.record()
-            self.gemm_timer.append((ev0, ev1, rows.shape[0]))
+            # rows the GEMM computed: every segment but the holes (weight matrix -1); read
+            # after the end event, so the copy is outside the timed launch
+            n = seg_offsets[1: num_seg + 1].long() - seg_offsets[:num_seg].long()
+            self.gemm_timer.append((ev0, ev1, int((n * (seg_expert[:num_seg] >= 0)).sum().item())))
         return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
                                       None, None, 0, max_rows, seg_expert)
 
