@@ -275,7 +275,9 @@ int lmoe_capacity_receive_plan(const int32_t* recv_counts, int ep, int experts_p
 /*                             (at ret_offset): lmoe_combine_rows with positions = slot       */
 /* state: int32[4] on the device, zeroed once ([0] step epoch, [1] error word: nonzero when a  */
 /* wait ran out of time or counts were inconsistent, [2], [3] internal counters).  Waits are  */
-/* bounded (2 s); every rank must run every step, in the same order.                          */
+/* bounded (2 s); every rank must run every step, in the same order.  lmoe_p2p_alloc / _free */
+/* / _open / _close are the library's only entry points that allocate, map or free device    */
+/* memory (and synchronise the device): call them at setup and teardown, never in a step.    */
 size_t lmoe_p2p_buffer_bytes(int ep, int num_experts, int64_t capacity_tokens, int top_k, int num_shared,
                              int hidden);
 int lmoe_p2p_buffer_offsets(int ep, int num_experts, int64_t capacity_tokens, int top_k, int num_shared,
@@ -297,6 +299,21 @@ int lmoe_p2p_wait(const uint64_t* peers, int me, int ep, int num_experts, int64_
 int lmoe_p2p_send_back(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
                        int num_shared, int hidden, int64_t num_tokens, int32_t* state, const void* out,
                        const int32_t* seg_offsets, lmoe_stream_t stream);
+
+/* Setup once after mapping the peers (shared experts' destinations in this rank's buffer).  */
+int lmoe_p2p_init(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
+                  int num_shared, int hidden, int32_t* state, lmoe_stream_t stream);
+/* The down projection fused with the return transfer (prefill-sized steps, in place of      */
+/* lmoe_p2p_send_back): the W4A16 grouped GEMM on h [rows region rows, ffn_size] (the gate/up */
+/* output of the rows region) whose epilogue writes each routed output row straight into its  */
+/* source rank's ret slot over NVLink and each shared-expert row into dest_bases[ep]          */
+/* ([S * num_tokens, hidden] bf16 of this rank); dest_bases[r < ep] = peers[r] + ret_offset. */
+/* Then the sources' return flags are raised.  buffer = this rank's own allocation.           */
+int lmoe_p2p_down_gemm(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens, int top_k,
+                       int num_shared, int hidden, int64_t num_tokens, int32_t* state, void* buffer,
+                       const void* h, int ffn_size, const uint8_t* w2_packed, int group_size,
+                       const int32_t* seg_offsets, const int32_t* seg_expert, int num_segments,
+                       int num_weight_matrices, const uint64_t* dest_bases, lmoe_stream_t stream);
 
 int lmoe_combine_rows(const void* rows, const int32_t* positions, const float* weights,
                       int64_t num_tokens, int top_k, int hidden_size,

@@ -46,6 +46,9 @@ SIGNATURES = {
     "lmoe_p2p_dispatch": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P]),
     "lmoe_p2p_wait": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _I, _P]),
     "lmoe_p2p_send_back": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _P]),
+    "lmoe_p2p_init": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _P, _P]),
+    "lmoe_p2p_down_gemm": (_I, [_P, _I, _I, _I, _I64, _I, _I, _I, _I64, _P, _P, _P, _I, _P, _I, _P, _P, _I,
+                                _I, _P, _P]),
     "lmoe_get_gemm_sm_limit": (_I, []),
     "lmoe_router_workspace_bytes": (_SZ, [_I64, _I]),
     "lmoe_router_workspace_bytes_typed": (_SZ, [_I64, _I, _I, _I]),

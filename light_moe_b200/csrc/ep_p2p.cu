@@ -8,7 +8,8 @@
 //   rows   [ep*Tc*k + S*Tc][d] bf16   rows for this rank's experts, expert-major (expert l:
 //                                     source 0's rows, source 1's, ...), then the shared
 //                                     experts' copies of this rank's own tokens at ep*Tc*k
-//   meta   [ep*Tc*k] int32  for each routed row: (source rank << 24) | source slot (t*k + j)
+//   meta   [ep*Tc*k + S*Tc] int32  for each routed row: (source rank << 24) | source slot
+//                                   (t*k + j); for shared row u: (ep << 24) | u (set once)
 //   ret    [Tc*k][d] bf16   this rank's own slots, each written back by the rank that ran it
 // (Tc = capacity tokens per rank and step, the same on every rank.)
 //
@@ -39,6 +40,7 @@
 
 #include <cstring>
 
+#include "grouped_gemm.h"
 #include "host_util.h"
 #include "ptx.cuh"
 
@@ -64,7 +66,7 @@ P2PLayout p2p_layout(int ep, int E, int64_t Tc, int k, int S, int d) {
   L.cnt = p; p = align256(p + sizeof(int32_t) * (size_t)ep * E);
   L.routed_rows = (int64_t)ep * Tc * k;
   L.rows = p; p = align256(p + sizeof(uint16_t) * (size_t)(L.routed_rows + (int64_t)S * Tc) * d);
-  L.meta = p; p = align256(p + sizeof(int32_t) * (size_t)L.routed_rows);
+  L.meta = p; p = align256(p + sizeof(int32_t) * (size_t)(L.routed_rows + (int64_t)S * Tc));
   L.ret = p; p = align256(p + sizeof(uint16_t) * (size_t)(Tc * k) * d);
   L.total = p;
   return L;
@@ -263,6 +265,25 @@ __global__ void __launch_bounds__(256) send_back_kernel(P2PArgs a, const uint4* 
   signal_when_grid_done(a, kFlagReturns, a.state + 3, epoch);
 }
 
+// Once: the shared rows' destinations, (ep << 24) | u for shared row u (buffer ep of the
+// down GEMM's destination table is this rank's shared-expert output).
+__global__ void init_meta_kernel(P2PArgs a) {
+  int32_t* meta = reinterpret_cast<int32_t*>(peer_base(a, a.me) + a.off_meta) + a.routed_rows;
+  const int64_t n = (int64_t)a.S * a.Tc;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < n; u += (int64_t)gridDim.x * blockDim.x)
+    meta[u] = (a.ep << 24) | (int32_t)u;
+}
+
+// After the down GEMM wrote its routed rows straight into the sources' ret regions: raise
+// the sources' return flags (the GEMM's stores are complete at its kernel boundary).
+__global__ void signal_returns_kernel(P2PArgs a) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t epoch = (uint32_t)a.state[0];
+    for (int r = 0; r < a.ep; ++r) st_release_sys(flag_ptr(a, r, kFlagReturns, a.me), epoch);
+  }
+}
+
 // Steps 3 and 5: wait until every peer raised flag `kind` for this step.
 __global__ void __launch_bounds__(64) wait_kernel(P2PArgs a, int kind) {
   wait_flags(a, kind, (uint32_t)a.state[0], kSite + 8 + kind);
@@ -419,5 +440,57 @@ extern "C" int lmoe_p2p_send_back(const uint64_t* peers, int me, int ep, int num
   const int grid = copy_grid(a.routed_rows);
   send_back_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(a, static_cast<const uint4*>(out),
                                                                                seg_offsets);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int lmoe_p2p_init(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens,
+                             int top_k, int num_shared, int hidden, int32_t* state, lmoe_stream_t stream_) {
+  P2PArgs a;
+  const int st = p2p_args(peers, me, ep, num_experts, capacity_tokens, top_k, num_shared, hidden, 0, state, &a);
+  if (st != LMOE_OK) return st;
+  if (num_shared == 0) return LMOE_OK;
+  const int64_t n = (int64_t)num_shared * capacity_tokens;
+  const int grid = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+  init_meta_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int lmoe_p2p_down_gemm(const uint64_t* peers, int me, int ep, int num_experts, int64_t capacity_tokens,
+                                  int top_k, int num_shared, int hidden, int64_t num_tokens, int32_t* state,
+                                  void* buffer, const void* h, int ffn_size, const uint8_t* w2_packed, int group_size,
+                                  const int32_t* seg_offsets, const int32_t* seg_expert, int num_segments,
+                                  int num_weight_matrices, const uint64_t* dest_bases, lmoe_stream_t stream_) {
+  P2PArgs a;
+  const int st = p2p_args(peers, me, ep, num_experts, capacity_tokens, top_k, num_shared, hidden, num_tokens, state,
+                          &a);
+  if (st != LMOE_OK) return st;
+  LMOE_ARG_CHECK(buffer && h && aligned16(h) && w2_packed && aligned16(w2_packed) && seg_offsets && seg_expert &&
+                 dest_bases);
+  LMOE_ARG_CHECK(num_segments >= 1 && num_weight_matrices >= 1 && ffn_size > 0);
+  const uint64_t own = reinterpret_cast<uint64_t>(buffer);   // this rank's buffer (= peers[me])
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  GemmProblem p;
+  p.x = h;
+  p.ldx = ffn_size;
+  p.total_rows = a.routed_rows + (int64_t)num_shared * capacity_tokens;
+  p.K = ffn_size;
+  p.offsets = seg_offsets;
+  p.num_experts = num_segments;
+  p.seg_expert = seg_expert;
+  p.num_w = num_weight_matrices;
+  p.wq = w2_packed;
+  p.group_size = group_size;
+  p.N = hidden;
+  p.mode = kModeScatter;
+  p.out = reinterpret_cast<void*>(own + a.off_ret);   // alignment reference; rows go through dest_bases
+  p.ldo = hidden;
+  p.dest = reinterpret_cast<const int32_t*>(own + a.off_meta);
+  p.dest_bases = dest_bases;
+  p.dest_count = ep + 1;
+  p.err = reinterpret_cast<uint32_t*>(state + 1);
+  p.max_rows_per_expert_hint = 0;
+  const int gs = run_grouped_gemm(p, stream);
+  if (gs != LMOE_OK) return gs;
+  signal_returns_kernel<<<1, 32, 0, stream>>>(a);
   return cuda_status(cudaGetLastError());
 }

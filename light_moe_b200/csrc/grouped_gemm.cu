@@ -84,7 +84,19 @@ struct GemmArgs {
   int num_w;                  // weight matrices available
   int64_t R;                  // activation rows
   int raster_rows;            // segments with more rows run token-block-major (tile_at)
+  // scatter to several buffers: dest[r] = (buffer << 24) | row of buffer dest_bases[buffer]
+  // (peer memory included: the outputs of an expert-parallel step go straight back to the
+  // rank that owns the token); NULL: dest[r] is a row of out
+  const uint64_t* dest_bases;
+  int dest_count;             // entries of dest_bases
 };
+
+// Output row base of a scattered row.
+__device__ __forceinline__ __nv_bfloat16* scatter_row(const GemmArgs& a, int32_t dest) {
+  if (a.dest_bases)
+    return reinterpret_cast<__nv_bfloat16*>(a.dest_bases[(uint32_t)dest >> 24]) + (int64_t)(dest & 0xffffff) * a.ldo;
+  return a.out + (int64_t)dest * a.ldo;
+}
 
 // fp32 -> the 16-bit output type (bf16, or fp16 for fp16 operands), as bf16 storage.
 __device__ __forceinline__ __nv_bfloat16 cvt_out(float v, int f16) {
@@ -503,7 +515,12 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
         for (int c = row; c < ti.rows; c += 128) {
           const int r = ti.row0 + c;
           tscale[c] = a.row_scale ? a.row_scale[r] : 1.0f;
-          tdest[c] = a.dest ? a.dest[r] : r;
+          int32_t dv = a.dest ? a.dest[r] : r;
+          if (a.dest_bases && (int)((uint32_t)dv >> 24) >= a.dest_count) {   // no such buffer: skip the row
+            report_error(a.err, kErrBadArg, kSite + 14);
+            dv = -1;
+          }
+          tdest[c] = dv;
         }
         named_bar_sync(2, 128);
       }
@@ -582,9 +599,10 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
           for (int j = 0; j < 4; ++j) {
             const int idx = row + 128 * j;    // 16-byte piece: token idx / 16, features 8 * (idx % 16) ..
             const int c = idx >> 4;
-            if (c0 + c < ti.rows) {
-              const int64_t orow = a.mode == kModeScatter ? (int64_t)tdest[c0 + c] : (int64_t)(ti.row0 + c0 + c);
-              *reinterpret_cast<uint4*>(a.out + orow * a.ldo + ti.fb * kBM + (idx & 15) * 8) =
+            if (c0 + c < ti.rows && (a.mode != kModeScatter || tdest[c0 + c] >= 0)) {
+              __nv_bfloat16* orow = a.mode == kModeScatter ? scatter_row(a, tdest[c0 + c])
+                                                           : a.out + (int64_t)(ti.row0 + c0 + c) * a.ldo;
+              *reinterpret_cast<uint4*>(orow + ti.fb * kBM + (idx & 15) * 8) =
                   *reinterpret_cast<const uint4*>(stg + c * kBM + (idx & 15) * 8);
             }
           }
@@ -595,14 +613,14 @@ __global__ void __launch_bounds__(Cfg<BN, DQ, WST, BST, AST, ACC, W4, BOX>::kThr
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int c = c0 + 16 * h + i;
-              if (c < ti.rows) {
+              if (c < ti.rows && (a.mode != kModeScatter || tdest[c] >= 0)) {
                 float val = __uint_as_float(h ? v1[i] : v0[i]);
-                int64_t orow = ti.row0 + c;
+                __nv_bfloat16* orow = a.out + (int64_t)(ti.row0 + c) * a.ldo;
                 if (a.mode == kModeScatter) {
                   if (a.row_scale) val = __fmul_rn(val, tscale[c]);
-                  orow = tdest[c];
+                  orow = scatter_row(a, tdest[c]);
                 }
-                a.out[orow * a.ldo + feat] = cvt_out(val, a.ab_f16);
+                orow[feat] = cvt_out(val, a.ab_f16);
               }
             }
           }
@@ -687,6 +705,8 @@ int run_grouped_gemm(const GemmProblem& p, cudaStream_t stream) {
   a.num_w = p.num_w > 0 ? p.num_w : p.num_experts;
   a.R = p.total_rows;
   a.raster_rows = w4 ? p.N / 4 : p.N;
+  a.dest_bases = p.mode == kModeScatter ? p.dest_bases : nullptr;
+  a.dest_count = p.dest_count;
 
   const bool small = p.max_rows_per_expert_hint > 0 && p.max_rows_per_expert_hint <= 64;
   // token-tile TMA box: 16 rows for decode-sized tiles (load only what the tile holds),

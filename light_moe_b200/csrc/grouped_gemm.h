@@ -39,6 +39,9 @@ struct GemmProblem {
   void* out = nullptr;
   int64_t ldo = 0;
   const int32_t* dest = nullptr;
+  // scatter into several buffers: dest[r] = (buffer << 24) | row of dest_bases[buffer]
+  const uint64_t* dest_bases = nullptr;
+  int dest_count = 0;
   const float* row_scale = nullptr;
   uint32_t* err = nullptr;
   // a known upper bound of rows per expert (0 = unknown); small values pick the decode tiles

@@ -130,6 +130,10 @@ class ExpertParallelGroup:
         return tensor
 
 
+# largest rows-per-expert bound for which the grouped GEMM entry point picks the decode kernels
+DECODE_MAX_ROWS = 64
+
+
 class CudaExpertBackend:
     """Local expert compute on the sm_100a library (the product path)."""
 
@@ -196,6 +200,13 @@ class CudaExpertBackend:
 
     def _experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         e = self.ex
+        h = self.gate_up(rows, seg_offsets, seg_expert, num_seg, max_rows)
+        return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
+                                      None, None, 0, max_rows, seg_expert)
+
+    def gate_up(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+        """The gate/up projection with the SwiGLU epilogue (h), timed when gemm_timer is set."""
+        e = self.ex
         if self.gemm_timer is not None:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev0.record()
@@ -208,8 +219,7 @@ class CudaExpertBackend:
             # after the end event, so the copy is outside the timed launch
             n = seg_offsets[1: num_seg + 1].long() - seg_offsets[:num_seg].long()
             self.gemm_timer.append((ev0, ev1, int((n * (seg_expert[:num_seg] >= 0)).sum().item())))
-        return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
-                                      None, None, 0, max_rows, seg_expert)
+        return h
 
     def combine(self, rows, positions, weights, T, extra, num_extra):
         return ops.combine_rows(rows, positions, weights, T, self.top_k, extra, num_extra)
@@ -349,15 +359,25 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         px.exchange_counts(counts, T)
         px.dispatch(x, sidx, ids, offsets)
         px.wait_rows(T)
-        out = be.experts(px.rows, px.seg_offsets, self._capacity_segments(dev), epr + 1 + S, self.capacity_tokens)
-        px.send_back(out, T)
+        segs, nseg = self._capacity_segments(dev), epr + 1 + S
+        if self.capacity_tokens > DECODE_MAX_ROWS:
+            # prefill-sized: the down GEMM's epilogue writes the routed rows straight into
+            # their sources' ret slots (the return transfer overlaps the GEMM's tiles)
+            h = be.gate_up(px.rows, px.seg_offsets, segs, nseg, self.capacity_tokens)
+            px.down_gemm(h, be.ex.w2_packed, be.ex.ffn_size, be.ex.group_size, segs, nseg, epr + S, T)
+            shared = px.shared_out
+        else:
+            # decode-sized: the decode GEMMs write locally, one copy kernel sends the rows back
+            out = be.experts(px.rows, px.seg_offsets, segs, nseg, self.capacity_tokens)
+            px.send_back(out, T)
+            shared = out[px.routed_rows:]
         px.wait_returns(T)
         if T == 0:
             return torch.empty(0, d, dtype=x.dtype, device=dev)
         key = ("slots", T * k, str(dev))
         if key not in self._seg_cache:
             self._seg_cache[key] = torch.arange(T * k, dtype=torch.int32, device=dev)
-        extra = out[px.routed_rows: px.routed_rows + S * T] if S else None
+        extra = shared[: S * T] if S else None
         return be.combine(px.ret[: T * k], self._seg_cache[key], w, T, extra, S)
 
     def close(self):

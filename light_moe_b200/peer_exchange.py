@@ -4,8 +4,9 @@ Each rank allocates one buffer with the library (``lmoe_p2p_alloc``: cudaMalloc 
 IPC handle), the handles are all-gathered once over the expert-parallel process group, and
 every rank maps its peers' buffers (``lmoe_p2p_open``).  From then on a step moves rows
 with the library's kernels only (``lmoe_p2p_exchange_counts``, ``lmoe_p2p_dispatch``,
-``lmoe_p2p_wait``, ``lmoe_p2p_send_back``): no NCCL call and no host synchronisation, so the
-whole step can be captured in a CUDA graph.  This replaces the NCCL all-to-alls of
+``lmoe_p2p_wait``, then ``lmoe_p2p_down_gemm`` -- the down projection whose epilogue writes
+each output row into its source's slot -- or ``lmoe_p2p_send_back``): no NCCL call and no
+host synchronisation, so the whole step can be captured in a CUDA graph.  This replaces the NCCL all-to-alls of
 python/light_moe/distributed/expert_parallel.py:186-244 and :275-319.
 """
 import ctypes
@@ -77,6 +78,13 @@ class PeerExchange:
         epr = num_experts // self.ep
         self.seg_offsets = torch.zeros(epr + 2 + S, dtype=torch.int32, device=device)
         self.dst_base = torch.zeros(num_experts, dtype=torch.int32, device=device)
+        # destinations of the fused down GEMM: every rank's ret region, then this rank's
+        # shared-expert outputs [S * T, d]
+        self.shared_out = torch.empty(max(S * Tc, 1), d, dtype=torch.bfloat16, device=device)
+        self.dest_bases = torch.tensor([b + ret_off.value for b in bases] + [self.shared_out.data_ptr()],
+                                       dtype=torch.int64, device=device)
+        capi.call("lmoe_p2p_init", self.peers.data_ptr(), self.me, self.ep, num_experts, Tc, k, S, d,
+                  self.state.data_ptr(), capi.stream_handle())
         torch.cuda.synchronize(device)
         dist.barrier(group=self.pg)   # every buffer is mapped before any rank writes to a peer
 
@@ -100,6 +108,14 @@ class PeerExchange:
     def send_back(self, out: torch.Tensor, num_tokens: int):
         capi.call("lmoe_p2p_send_back", *self._args(num_tokens), out.data_ptr(), self.seg_offsets.data_ptr(),
                   capi.stream_handle())
+
+    def down_gemm(self, h: torch.Tensor, w2_packed: torch.Tensor, ffn_size: int, group_size: int,
+                  seg_expert: torch.Tensor, num_segments: int, num_weight_matrices: int, num_tokens: int):
+        """The down projection of the rows region with the return transfer fused into its
+        epilogue (routed rows straight into their sources' ret slots), then the return flags."""
+        capi.call("lmoe_p2p_down_gemm", *self._args(num_tokens), self._own, h.data_ptr(), ffn_size,
+                  w2_packed.data_ptr(), group_size, self.seg_offsets.data_ptr(), seg_expert.data_ptr(),
+                  num_segments, num_weight_matrices, self.dest_bases.data_ptr(), capi.stream_handle())
 
     def wait_returns(self, num_tokens: int):
         capi.call("lmoe_p2p_wait", *self._args(num_tokens), 2, capi.stream_handle())
