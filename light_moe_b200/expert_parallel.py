@@ -224,6 +224,18 @@ class CudaExpertBackend:
     def combine(self, rows, positions, weights, T, extra, num_extra):
         return ops.combine_rows(rows, positions, weights, T, self.top_k, extra, num_extra)
 
+    def make_exchange(self, group, config, capacity_tokens):
+        """The peer-memory exchange (symmetric buffers mapped over CUDA IPC; collective)."""
+        from .peer_exchange import PeerExchange
+        return PeerExchange(group, config.num_experts, capacity_tokens, config.top_k, config.num_shared,
+                            config.hidden_size, torch.device("cuda", torch.cuda.current_device()))
+
+    def down_to_peers(self, px, h, seg_expert, num_seg, num_tokens):
+        """The down projection whose epilogue returns every routed row to its source's slot."""
+        e = self.ex
+        px.down_gemm(h, e.w2_packed, e.ffn_size, e.group_size, seg_expert, num_seg, self.num_local + self.num_shared,
+                     num_tokens)
+
 
 class ExpertParallelW4A16Layer(torch.nn.Module):
     """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks."""
@@ -261,12 +273,9 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         # buffers here, outside any CUDA graph capture)
         self.exchange = None
         if dispatch == "p2p":
-            if not isinstance(backend, CudaExpertBackend):
-                raise ValueError("p2p dispatch runs on the CUDA expert backend only")
-            from .peer_exchange import PeerExchange
-            self.exchange = PeerExchange(ep_group, config.num_experts, self.capacity_tokens, config.top_k,
-                                         config.num_shared, config.hidden_size,
-                                         torch.device("cuda", torch.cuda.current_device()))
+            if not hasattr(backend, "make_exchange"):
+                raise ValueError("p2p dispatch needs a backend that provides the peer exchange")
+            self.exchange = backend.make_exchange(ep_group, config, self.capacity_tokens)
 
     @classmethod
     def from_full(cls, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
@@ -364,7 +373,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             # prefill-sized: the down GEMM's epilogue writes the routed rows straight into
             # their sources' ret slots (the return transfer overlaps the GEMM's tiles)
             h = be.gate_up(px.rows, px.seg_offsets, segs, nseg, self.capacity_tokens)
-            px.down_gemm(h, be.ex.w2_packed, be.ex.ffn_size, be.ex.group_size, segs, nseg, epr + S, T)
+            be.down_to_peers(px, h, segs, nseg, T)
             shared = px.shared_out
         else:
             # decode-sized: the decode GEMMs write locally, one copy kernel sends the rows back

@@ -62,3 +62,106 @@ class OracleExpertBackend:
         for s in range(num_extra):
             y += extra[s * T:(s + 1) * T]
         return y
+
+    # --- peer-memory exchange (dispatch="p2p"), restated on CPU ranks -----------------
+    def make_exchange(self, group, config, capacity_tokens):
+        return EmulatedPeerExchange(group, config.num_experts, capacity_tokens, config.top_k, config.num_shared,
+                                    config.hidden_size)
+
+    def gate_up(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+        return rows   # the whole expert MLP runs in down_to_peers
+
+    def down_to_peers(self, px, h, seg_expert, num_seg, num_tokens):
+        out = self.experts(h, px.seg_offsets, seg_expert, num_seg, None)
+        px.send_back(out, num_tokens)
+        S, T = self.num_shared, num_tokens
+        if S:
+            px.shared_out[: S * T] = out[px.routed_rows: px.routed_rows + S * T]
+
+
+class EmulatedPeerExchange:
+    """The peer-memory exchange of light_moe_b200/csrc/ep_p2p.cu restated for CPU ranks: the
+    same buffer regions (rows expert-major by source, meta words, returned slots, shared
+    rows), the same count-matrix arithmetic for segment offsets and destination positions,
+    with gloo all-to-alls standing in for the peer stores.  Test infrastructure only."""
+
+    def __init__(self, group, num_experts, capacity_tokens, top_k, num_shared, hidden):
+        import torch.distributed as dist
+        self.dist = dist
+        self.pg = group.group
+        self.ep, self.me = group.ep_size, group.rank
+        self.E, self.Tc, self.k, self.S, self.d = num_experts, int(capacity_tokens), top_k, num_shared, hidden
+        self.epr = num_experts // self.ep
+        self.routed_rows = self.ep * self.Tc * top_k
+        self.rows = torch.zeros(self.routed_rows + num_shared * self.Tc, hidden)
+        self.meta = torch.zeros(self.routed_rows + num_shared * self.Tc, dtype=torch.int64)
+        self.meta[self.routed_rows:] = (self.ep << 24) + torch.arange(num_shared * self.Tc)
+        self.ret = torch.zeros(self.Tc * top_k, hidden)
+        self.shared_out = torch.zeros(max(num_shared * self.Tc, 1), hidden)
+        self.seg_offsets = torch.zeros(self.epr + 2 + num_shared, dtype=torch.int32)
+        self.dst_base = torch.zeros(num_experts, dtype=torch.int64)
+
+    def exchange_counts(self, counts, num_tokens):
+        ep, E, epr, me = self.ep, self.E, self.epr, self.me
+        mine = counts.to(torch.int64).reshape(E)
+        allc = [torch.empty_like(mine) for _ in range(ep)]
+        self.dist.all_gather(allc, mine, group=self.pg)
+        cnt = torch.stack(allc)                                   # [source, expert]
+        per_expert = cnt.sum(0)
+        seg = [0]
+        for l in range(epr):
+            seg.append(seg[-1] + int(per_expert[me * epr + l]))
+        seg.append(self.routed_rows)
+        seg += [self.routed_rows + (s + 1) * num_tokens for s in range(self.S)]
+        self.seg_offsets = torch.tensor(seg, dtype=torch.int32)
+        for e in range(E):
+            r = e // epr
+            self.dst_base[e] = int(per_expert[r * epr: e].sum()) + int(cnt[:me, e].sum())
+
+    def _exchange(self, dest_rank, payload_rows, payload_idx):
+        """Send payload rows / indices to their destination ranks; returns what arrived."""
+        order = torch.argsort(dest_rank, stable=True)
+        send_n = torch.bincount(dest_rank, minlength=self.ep)
+        recv_n = torch.empty_like(send_n)
+        self.dist.all_to_all_single(recv_n, send_n, group=self.pg)
+        rows_in = torch.empty(int(recv_n.sum()), self.d)
+        idx_in = torch.empty(int(recv_n.sum()), payload_idx.shape[1], dtype=torch.int64)
+        self.dist.all_to_all_single(rows_in, payload_rows[order].contiguous(), recv_n.tolist(), send_n.tolist(),
+                                    group=self.pg)
+        self.dist.all_to_all_single(idx_in, payload_idx[order].contiguous(), recv_n.tolist(), send_n.tolist(),
+                                    group=self.pg)
+        return rows_in, idx_in
+
+    def dispatch(self, x, sorted_idx, ids, offsets):
+        T, k = x.shape[0], self.k
+        if T:
+            f = sorted_idx.long()
+            e = ids.reshape(-1).long()[f]
+            pos = self.dst_base[e] + (torch.arange(T * k) - offsets.long()[e])
+            meta = (self.me << 24) + f
+            rows_in, idx_in = self._exchange(e // self.epr, x[f // k], torch.stack([pos, meta], 1))
+        else:
+            rows_in, idx_in = self._exchange(torch.zeros(0, dtype=torch.int64), torch.zeros(0, self.d),
+                                             torch.zeros(0, 2, dtype=torch.int64))
+        self.rows[idx_in[:, 0]] = rows_in
+        self.meta[idx_in[:, 0]] = idx_in[:, 1]
+        for s in range(self.S):
+            self.rows[self.routed_rows + s * T: self.routed_rows + (s + 1) * T] = x
+
+    def wait_rows(self, num_tokens):
+        pass
+
+    def send_back(self, out, num_tokens):
+        R = int(self.seg_offsets[self.epr])
+        m = self.meta[:R]
+        rows_in, idx_in = self._exchange(m >> 24, out[:R], (m & 0xFFFFFF)[:, None])
+        self.ret[idx_in[:, 0]] = rows_in
+
+    def wait_returns(self, num_tokens):
+        pass
+
+    def error(self):
+        return 0
+
+    def close(self):
+        pass
