@@ -3,8 +3,10 @@
  *
  * Plain pointers, sizes and a CUDA stream; no framework types.  Every entry point:
  *   - launches asynchronously on `stream` (never on the legacy default stream unless the
- *     caller passes it) and performs no host<->device synchronisation;
- *   - never allocates device memory: outputs and workspaces are caller-owned;
+ *     caller passes it) and performs no host<->device synchronisation (except the
+ *     peer-exchange setup and teardown, lmoe_p2p_alloc / _free);
+ *   - never allocates device memory: outputs and workspaces are caller-owned (the one
+ *     exception is the peer-exchange setup, lmoe_p2p_alloc / _open, run once per layer);
  *   - returns LMOE_OK (0), a negative LMOE_ERR_* for rejected arguments, or a positive
  *     cudaError_t value when a CUDA call failed.
  * Kernels that wait on their own pipelines bound every wait; a wait that gives up writes a
