@@ -187,22 +187,25 @@ class CudaExpertBackend:
                   restore.data_ptr(), seg_offsets.data_ptr(), capi.stream_handle())
         return regroup, restore, seg_offsets
 
-    def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+    def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows, down_max_rows=None):
+        """Both projections of the segments.  max_rows / down_max_rows: the rows-per-segment
+        hints of the gate/up and down GEMMs (<= 64 selects the decode kernels)."""
         if self.sm_limit is None:
-            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows)
+            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows, down_max_rows)
         from . import capi
         prev = capi.lib().lmoe_get_gemm_sm_limit()
         capi.call("lmoe_set_gemm_sm_limit", int(self.sm_limit))
         try:
-            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows)
+            return self._experts(rows, seg_offsets, seg_expert, num_seg, max_rows, down_max_rows)
         finally:
             capi.call("lmoe_set_gemm_sm_limit", prev)
 
-    def _experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+    def _experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows, down_max_rows=None):
         e = self.ex
         h = self.gate_up(rows, seg_offsets, seg_expert, num_seg, max_rows)
         return ops.w4a16_grouped_gemm(h, e.w2_packed, seg_offsets, num_seg, e.hidden_size, e.group_size, 0,
-                                      None, None, 0, max_rows, seg_expert)
+                                      None, None, 0, max_rows if down_max_rows is None else down_max_rows,
+                                      seg_expert)
 
     def gate_up(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
         """The gate/up projection with the SwiGLU epilogue (h), timed when gemm_timer is set."""
@@ -302,6 +305,21 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
             self._seg_cache[key] = torch.tensor(seg, dtype=torch.int32, device=device)
         return self._seg_cache[key]
 
+    def _gemm_hints(self):
+        """Rows-per-segment hints of the gate/up and down GEMMs of a capacity-bounded step,
+        from the expected rows per local expert (ep * Tc * k / E; the segments' real sizes
+        stay on the device).  Measured on one Mixtral expert (gate/up 28672 x 4096, down 4096 x
+        14336) as a single segment: the decode kernel
+        (32-row token blocks, the weights streamed once per block) wins the gate/up GEMM up
+        to ~32 rows (39 against 50 us) and loses from 64 (68 against 52; 113 against 56 at
+        128); its down GEMM wins up to 128 rows (55 against 82 us) and loses from ~192."""
+        cfg = self.config
+        est = self.ep_group.ep_size * self.capacity_tokens * cfg.top_k // cfg.num_experts
+        big = max(est, DECODE_MAX_ROWS + 1)
+        gu = DECODE_MAX_ROWS if est < DECODE_MAX_ROWS else big
+        dn = DECODE_MAX_ROWS if est <= 2 * DECODE_MAX_ROWS else big
+        return gu, dn
+
     def _capacity_segments(self, device):
         key = ("cap", str(device))
         if key not in self._seg_cache:
@@ -340,7 +358,7 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         rows_em[: ep * C] = be.take(recv, regroup)
         for s in range(S):
             rows_em[ep * C + s * T: ep * C + (s + 1) * T].copy_(x)
-        out_em = be.experts(rows_em, seg_offsets, self._capacity_segments(dev), epr + 1 + S, self.capacity_tokens)
+        out_em = be.experts(rows_em, seg_offsets, self._capacity_segments(dev), epr + 1 + S, *self._gemm_hints())
         out = be.take(out_em, restore)                                              # back to capacity order
         ret = torch.empty(ep * C, d, dtype=x.dtype, device=dev)
         g.all_to_all(ret, out)
@@ -369,15 +387,16 @@ class ExpertParallelW4A16Layer(torch.nn.Module):
         px.dispatch(x, sidx, ids, offsets)
         px.wait_rows(T)
         segs, nseg = self._capacity_segments(dev), epr + 1 + S
-        if self.capacity_tokens > DECODE_MAX_ROWS:
-            # prefill-sized: the down GEMM's epilogue writes the routed rows straight into
+        gu_hint, dn_hint = self._gemm_hints()
+        if dn_hint > DECODE_MAX_ROWS:
+            # large segments: the down GEMM's epilogue writes the routed rows straight into
             # their sources' ret slots (the return transfer overlaps the GEMM's tiles)
-            h = be.gate_up(px.rows, px.seg_offsets, segs, nseg, self.capacity_tokens)
+            h = be.gate_up(px.rows, px.seg_offsets, segs, nseg, gu_hint)
             be.down_to_peers(px, h, segs, nseg, T)
             shared = px.shared_out
         else:
-            # decode-sized: the decode GEMMs write locally, one copy kernel sends the rows back
-            out = be.experts(px.rows, px.seg_offsets, segs, nseg, self.capacity_tokens)
+            # decode-sized down GEMM (writes locally), then one copy kernel sends the rows back
+            out = be.experts(px.rows, px.seg_offsets, segs, nseg, gu_hint, dn_hint)
             px.send_back(out, T)
             shared = out[px.routed_rows:]
         px.wait_returns(T)

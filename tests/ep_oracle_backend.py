@@ -42,7 +42,7 @@ class OracleExpertBackend:
     def take(self, rows, index):
         return rows[index.long()].contiguous()
 
-    def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows):
+    def experts(self, rows, seg_offsets, seg_expert, num_seg, max_rows, down_max_rows=None):
         out = torch.zeros(rows.shape[0], self.w2.shape[1], dtype=rows.dtype)
         off = seg_offsets.tolist()
         se = seg_expert.tolist()

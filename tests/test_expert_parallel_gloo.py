@@ -125,7 +125,7 @@ def _run(world, case, timeout=120):
     (2, dict(E=8, S=0, k=2, d=64, F=64, g=64, T=[16, 16], dispatch="p2p", cap=16)),
     (4, dict(E=8, S=1, k=3, d=64, F=64, g=64, T=[30, 0, 12, 1], dispatch="p2p", cap=32)),
     (4, dict(E=64, S=2, k=6, d=64, F=64, g=64, T=[9, 3, 8, 2], dispatch="p2p", cap=9)),
-    (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[90, 70], dispatch="p2p", cap=96)),
+    (2, dict(E=8, S=1, k=2, d=64, F=128, g=64, T=[290, 70], dispatch="p2p", cap=300)),
 ])
 def test_expert_parallel_matches_single_process(world, case):
     results, codes = _run(world, case)

@@ -110,10 +110,12 @@ CASES = [dict(E=8, S=0, k=2, d=512, F=256, g=128, T=[300, 77]),
          dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64], dispatch="capacity", cap=64),
          dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="capacity", cap=40),
          # rows through peer memory: Mixtral decode shape, shared experts with ragged tokens,
-         # and prefill-sized steps (grouped GEMM tiles)
+         # prefill gate/up tiles with the decode down GEMM (~75 rows per expert), and the
+         # down GEMM writing to the peers (~150 rows per expert)
          dict(E=8, S=0, k=2, d=4096, F=14336, g=128, T=[64, 64], dispatch="p2p", cap=64),
          dict(E=16, S=2, k=4, d=256, F=128, g=64, T=[10, 33], bias=True, dispatch="p2p", cap=40),
-         dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[300, 77], dispatch="p2p", cap=300)]
+         dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[300, 77], dispatch="p2p", cap=300),
+         dict(E=8, S=1, k=2, d=512, F=256, g=128, T=[600, 77], dispatch="p2p", cap=600)]
 
 
 @pytest.mark.parametrize("case", CASES)
