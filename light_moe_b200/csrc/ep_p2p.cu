@@ -26,10 +26,12 @@
 //   4. send_back        every routed output row goes straight into its source rank's ret
 //                       slot; the last CTA raises the sources' return flags
 //   5. wait(returns)    then the weighted combine reads ret locally
-// Buffers are single: a peer writes step e+1 data into this rank's buffers only after it
-// finished step e, which needed this rank's returned rows of step e, sent after this rank's
-// last read of its rows (the down GEMM) and after its step-e combine... so no step's data
-// is overwritten while it is read.  Flags only grow (epochs), so a wait is "flag >= epoch".
+// Buffers are single.  A peer writes this rank's count matrix, rows and meta for step e+1
+// only after finishing its step e, which needed this rank's returned rows of step e, sent
+// after this rank's last reads of them (counts exchange, down GEMM, send-back).  It writes
+// this rank's ret region for step e+1 only after receiving this rank's step-e+1 rows, which
+// this rank dispatches after its step-e combine.  So no data is overwritten while it is
+// read.  Flags only grow (epochs), so a wait is "flag >= epoch".
 //
 // Reference: the exchange of python/light_moe/distributed/expert_parallel.py:186-244 and
 // :275-319 (padded NCCL all-to-alls of whole token sets); here only routed rows move, once
