@@ -104,8 +104,24 @@ class W4A16MoELayer(torch.nn.Module):
         ``SMALL_BATCH_TOKENS`` tokens (a batch that small is one range), so each range runs
         the same kernels as the whole batch would and the result is bit-identical to
         ``forward(x_host.cuda()).cpu()``.  Returns ``out``; it is complete once the current
-        CUDA stream has reached the point of return (synchronise before reading it).
+        CUDA stream has reached the point of return (synchronise before reading it).  The
+        input copies of a call start at once, beside the previous call's kernels.
         """
+        out, done = self.forward_host_async(x_host, out, chunks)
+        if done is not None:
+            torch.cuda.current_stream(self.gate_weight.device).wait_event(done)
+        return out
+
+    def forward_host_async(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
+                           chunks: Optional[int] = None):
+        """forward_host without the current stream waiting for the output copies: returns
+        (out, done), ``done`` a CUDA event recorded after the last device-to-host copy
+        (``done.synchronize()``, or make a stream wait on it, before reading ``out``; None for
+        an empty batch).  In a
+        loop of calls the output copies of one call overlap the next call's kernels, and its
+        input copies the previous call's kernels; calls keep their order on every stream, so
+        consecutive calls may reuse the same ``out`` and ``x_host``.  Same results as
+        forward_host."""
         if x_host.device.type != "cpu":
             raise ValueError("forward_host takes host activations; use forward for device tensors")
         if x_host.dtype != torch.bfloat16:
@@ -121,27 +137,29 @@ class W4A16MoELayer(torch.nn.Module):
         y2 = out.view(-1, shape[-1])
         T = x2.shape[0]
         if T == 0:
-            return out
+            return out, None   # nothing to copy or compute
         device = self.gate_weight.device
         cur = torch.cuda.current_stream(device)
+        if not hasattr(self, "_copy_streams"):
+            self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        h2d, d2h = self._copy_streams
+        done = torch.cuda.Event()
         if chunks is None:
             chunks = min(4, T // 2560)
         n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
         bounds = [T * i // n for i in range(n + 1)]
-        if not hasattr(self, "_copy_streams"):
-            self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
-        h2d, d2h = self._copy_streams
-        xd = torch.empty((T, shape[-1]), dtype=torch.bfloat16, device=device)
-        h2d.wait_stream(cur)            # xd's memory is free on the current stream from here
         loaded = []
         with torch.cuda.stream(h2d):
+            # the staging buffer belongs to the copy stream (its memory is free there), so the
+            # copies start without waiting for the current stream's earlier work
+            xd = torch.empty((T, shape[-1]), dtype=torch.bfloat16, device=device)
             for i in range(n):
                 a, b = bounds[i], bounds[i + 1]
                 xd[a:b].copy_(x2[a:b], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(h2d)
                 loaded.append(ev)
-        xd.record_stream(h2d)
+        xd.record_stream(cur)
         for i in range(n):
             a, b = bounds[i], bounds[i + 1]
             cur.wait_event(loaded[i])
@@ -150,5 +168,5 @@ class W4A16MoELayer(torch.nn.Module):
             with torch.cuda.stream(d2h):
                 y2[a:b].copy_(yc, non_blocking=True)
             yc.record_stream(d2h)
-        cur.wait_stream(d2h)
-        return out
+        done.record(d2h)
+        return out, done

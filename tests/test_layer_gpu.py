@@ -138,3 +138,34 @@ def test_forward_host_matches_forward(T, chunks):
     assert torch.equal(out.view(T, d).view(torch.int16), y_dev.view(torch.int16))
     with pytest.raises(ValueError):
         mod.forward_host(x, chunks=chunks)   # device input belongs to forward
+
+
+def test_forward_host_async_back_to_back_calls():
+    """Consecutive host-buffer calls without waiting in between (the next call's input copies
+    beside this call's kernels, this call's output copies beside the next call's kernels):
+    each output equals the device call on its own input, also when two calls share one
+    output buffer and the first result is read before the second call overwrites it."""
+    d, F, E, k, g = 256, 256, 8, 2, 128
+    T = 3000
+    xs, refs = [], []
+    x0, gw, ex, _ = _make(T, d, F, E, k, g, seed=11)
+    mod = W4A16MoELayer(gw, ex, k)
+    for i in range(3):
+        x = x0 if i == 0 else torch.randn(T, d, generator=torch.Generator().manual_seed(50 + i)).to(
+            torch.bfloat16).cuda()
+        xs.append(x.cpu().pin_memory())
+        refs.append(mod(x).cpu())
+    outs = [torch.empty(T, d, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    events = [mod.forward_host_async(xs[i], out=outs[i], chunks=3)[1] for i in range(3)]
+    for i in range(3):
+        events[i].synchronize()
+        assert torch.equal(outs[i].view(torch.int16), refs[i].view(torch.int16)), i
+    # one shared output buffer: the stream order keeps each result until the next call's copy
+    shared = torch.empty(T, d, dtype=torch.bfloat16).pin_memory()
+    _, ev = mod.forward_host_async(xs[1], out=shared, chunks=3)
+    ev.synchronize()
+    first = shared.clone()
+    _, ev = mod.forward_host_async(xs[2], out=shared, chunks=3)
+    ev.synchronize()
+    assert torch.equal(first.view(torch.int16), refs[1].view(torch.int16))
+    assert torch.equal(shared.view(torch.int16), refs[2].view(torch.int16))
