@@ -595,8 +595,7 @@ def run_ours(args):
                        "l2": l2_note(ex, ws, T)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                     "d2h_bytes_per_step": T * D * 2,
-                    "call": ("W4A16MoELayer.forward_host_async called back to back (pinned host buffers; "
-                             "the copies of one token range overlap the kernels of the next, and a call's "
+                    "call": ("W4A16MoELayer.forward_host_async called back to back (pinned host buffers; a call's "
                              "input / output copies overlap the previous / next call's kernels); timed from "
                              "before the first input copy to after the last output copy" if ws == 1 else
                              "pinned host x -> device, ExpertParallelW4A16Layer.forward, y -> pinned host")},

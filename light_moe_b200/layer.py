@@ -107,13 +107,15 @@ class W4A16MoELayer(torch.nn.Module):
         CUDA stream has reached the point of return (synchronise before reading it).  The
         input copies of a call start at once, beside the previous call's kernels.
         """
+        if chunks is None:   # one call on its own: hide the copies behind its own token ranges
+            chunks = min(4, x_host.reshape(-1, x_host.shape[-1]).shape[0] // 2560)
         out, done = self.forward_host_async(x_host, out, chunks)
         if done is not None:
             torch.cuda.current_stream(self.gate_weight.device).wait_event(done)
         return out
 
     def forward_host_async(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
-                           chunks: Optional[int] = None):
+                           chunks: int = 1):
         """forward_host without the current stream waiting for the output copies: returns
         (out, done), ``done`` a CUDA event recorded after the last device-to-host copy
         (``done.synchronize()``, or make a stream wait on it, before reading ``out``; None for
@@ -121,7 +123,10 @@ class W4A16MoELayer(torch.nn.Module):
         loop of calls the output copies of one call overlap the next call's kernels, and its
         input copies the previous call's kernels; calls keep their order on every stream, so
         consecutive calls may reuse the same ``out`` and ``x_host``.  Same results as
-        forward_host."""
+        forward_host.  ``chunks`` defaults to one token range: in a loop of calls the
+        neighbouring calls' kernels already hide the copies, and whole-batch GEMM tiles are
+        fuller (8192 tokens of the Mixtral layer: 5.42-5.50 ms per call against 5.78-5.86
+        with 2-3 ranges, 5.24 ms device-only)."""
         if x_host.device.type != "cpu":
             raise ValueError("forward_host takes host activations; use forward for device tensors")
         if x_host.dtype != torch.bfloat16:
@@ -144,8 +149,6 @@ class W4A16MoELayer(torch.nn.Module):
             self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
         h2d, d2h = self._copy_streams
         done = torch.cuda.Event()
-        if chunks is None:
-            chunks = min(4, T // 2560)
         n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
         bounds = [T * i // n for i in range(n + 1)]
         loaded = []
