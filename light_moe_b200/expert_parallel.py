@@ -56,7 +56,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layer import W4A16Experts
+from .layer import HostBufferCalls, W4A16Experts
 
 
 @dataclass
@@ -240,8 +240,12 @@ class CudaExpertBackend:
                      num_tokens)
 
 
-class ExpertParallelW4A16Layer(torch.nn.Module):
-    """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks."""
+class ExpertParallelW4A16Layer(HostBufferCalls, torch.nn.Module):
+    """Expert-parallel W4A16 MoE layer: experts sharded by contiguous blocks over ep ranks.
+    forward_host / forward_host_async (host-resident activations) run every call as one token
+    range, so all ranks take the same steps."""
+
+    _host_ranges = False
 
     def __init__(self, config: ExpertParallelConfig, ep_group: ExpertParallelGroup, gate_weight: torch.Tensor,
                  backend, gate_bias: Optional[torch.Tensor] = None, micro_batches: int = 1,

@@ -68,27 +68,13 @@ class W4A16Experts:
         return cls(w13p, w2p, num_experts, Et - num_experts, d, F, group_size, canon)
 
 
-class W4A16MoELayer(torch.nn.Module):
-    """y = sum_j w_j * expert_{e_j}(x)  (+ shared experts), int4 experts, bf16 activations."""
+class HostBufferCalls:
+    """forward_host / forward_host_async for a layer module whose ``forward`` runs on the
+    device of ``self.gate_weight``: host-resident activations in, host-resident outputs out,
+    the PCIe copies on two copy streams beside the kernels.  ``_host_ranges`` False keeps
+    every call one token range (a layer whose ranks must all run the same number of steps)."""
 
-    def __init__(self, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
-                 gate_bias: Optional[torch.Tensor] = None):
-        super().__init__()
-        if gate_weight.shape != (experts.num_experts, experts.hidden_size):
-            raise ValueError("gate_weight must be [num_experts, hidden_size]")
-        self.register_buffer("gate_weight", gate_weight.to(torch.bfloat16).contiguous())
-        self.register_buffer("gate_bias", None if gate_bias is None else gate_bias.float().contiguous())
-        self.experts = experts
-        self.top_k = int(top_k)
-
-    def forward(self, x: torch.Tensor, return_routing: bool = False):
-        shape = x.shape
-        x2 = x.reshape(-1, shape[-1])
-        e = self.experts
-        y, ids, w = ops.moe_layer_w4a16(x2, self.gate_weight, e.w13_packed, e.w2_packed, self.top_k,
-                                        e.ffn_size, e.group_size, e.num_shared, self.gate_bias)
-        y = y.view(*shape[:-1], shape[-1])
-        return (y, ids, w) if return_routing else y
+    _host_ranges = True
 
     def forward_host(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
                      chunks: Optional[int] = None) -> torch.Tensor:
@@ -108,7 +94,7 @@ class W4A16MoELayer(torch.nn.Module):
         input copies of a call start at once, beside the previous call's kernels.
         """
         if chunks is None:   # one call on its own: hide the copies behind its own token ranges
-            chunks = min(4, x_host.reshape(-1, x_host.shape[-1]).shape[0] // 2560)
+            chunks = min(4, x_host.reshape(-1, x_host.shape[-1]).shape[0] // 2560) if self._host_ranges else 1
         out, done = self.forward_host_async(x_host, out, chunks)
         if done is not None:
             torch.cuda.current_stream(self.gate_weight.device).wait_event(done)
@@ -141,14 +127,16 @@ class W4A16MoELayer(torch.nn.Module):
             raise ValueError("out must be contiguous")
         y2 = out.view(-1, shape[-1])
         T = x2.shape[0]
-        if T == 0:
-            return out, None   # nothing to copy or compute
+        if T == 0 and self._host_ranges:
+            return out, None   # nothing to copy or compute (a multi-rank layer still takes its step)
         device = self.gate_weight.device
         cur = torch.cuda.current_stream(device)
         if not hasattr(self, "_copy_streams"):
             self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
         h2d, d2h = self._copy_streams
         done = torch.cuda.Event()
+        if not self._host_ranges and chunks != 1:
+            raise ValueError("this layer runs every call as one token range (chunks=1)")
         n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
         bounds = [T * i // n for i in range(n + 1)]
         loaded = []
@@ -173,3 +161,27 @@ class W4A16MoELayer(torch.nn.Module):
             yc.record_stream(d2h)
         done.record(d2h)
         return out, done
+
+
+class W4A16MoELayer(HostBufferCalls, torch.nn.Module):
+    """y = sum_j w_j * expert_{e_j}(x)  (+ shared experts), int4 experts, bf16 activations."""
+
+    def __init__(self, gate_weight: torch.Tensor, experts: W4A16Experts, top_k: int,
+                 gate_bias: Optional[torch.Tensor] = None):
+        super().__init__()
+        if gate_weight.shape != (experts.num_experts, experts.hidden_size):
+            raise ValueError("gate_weight must be [num_experts, hidden_size]")
+        self.register_buffer("gate_weight", gate_weight.to(torch.bfloat16).contiguous())
+        self.register_buffer("gate_bias", None if gate_bias is None else gate_bias.float().contiguous())
+        self.experts = experts
+        self.top_k = int(top_k)
+
+    def forward(self, x: torch.Tensor, return_routing: bool = False):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        e = self.experts
+        y, ids, w = ops.moe_layer_w4a16(x2, self.gate_weight, e.w13_packed, e.w2_packed, self.top_k,
+                                        e.ffn_size, e.group_size, e.num_shared, self.gate_bias)
+        y = y.view(*shape[:-1], shape[-1])
+        return (y, ids, w) if return_routing else y
+

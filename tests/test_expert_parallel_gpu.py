@@ -54,6 +54,12 @@ def _worker(rank, world, port, case, q):
         y_ref = ref_layer(x)
         torch.cuda.synchronize()
         err = ((y.float() - y_ref.float()).abs().max() / y_ref.float().abs().max()).item()
+        # host-resident activations (every rank calls, one token range per call): the same bits
+        if case.get("mb", 1) == 1:
+            yh, done = ep_layer.forward_host_async(x.cpu().pin_memory())
+            done.synchronize()
+            if not torch.equal(yh.view(torch.int16), y.cpu().view(torch.int16)):
+                err = float("inf")
         if case.get("dispatch") in ("capacity", "p2p"):
             # the whole step (router, gather / peer copies, exchanges, GEMMs, combine) in one graph
             side = torch.cuda.Stream()
