@@ -176,7 +176,9 @@ def time_host_calls(layer, xh, yh, steps, warmup, stream, barrier=None):
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    layer._copy_streams[0].wait_event(ev0)   # the first input copy starts after ev0
+    streams = getattr(layer, "_copy_streams", None)
+    if streams is not None:
+        streams[0].wait_event(ev0)           # the first input copy starts after ev0
     for _ in range(steps):
         _, done = layer.forward_host_async(xh, out=yh)
     stream.wait_event(done)                  # ... and ev1 after the last output copy
@@ -517,9 +519,9 @@ def run_ours(args):
     secs = t.item()
     value = T * ws * args.steps / secs
 
-    # end to end through the public API: pinned host x -> device, layer, y -> pinned host.
-    # One GPU: the layer's host-buffer call, which overlaps the copies of one token range
-    # with the kernels of the next; expert parallel: copy in, forward, copy out.
+    # end to end through the public API: pinned host x -> device, layer, y -> pinned host,
+    # with the layer's asynchronous host-buffer calls back to back (one GPU and expert
+    # parallel alike): a call's copies overlap the neighbouring calls' kernels.
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
 
