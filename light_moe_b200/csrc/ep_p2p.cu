@@ -104,6 +104,22 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// One warp copies one row of `vec` 16-byte words, eight loads per lane in flight before
+// their stores (a load-then-store chain per word would pay a memory round trip each).
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int vec,
+                                         int lane) {
+  constexpr int kU = 8;
+  for (int c0 = lane; c0 < vec; c0 += 32 * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (c0 + 32 * u < vec) v[u] = __ldg(src + c0 + 32 * u);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (c0 + 32 * u < vec) dst[c0 + 32 * u] = v[u];
+  }
+}
+
 // Threads 0..ep-1 each wait for the flag of one source rank to reach the epoch (bounded);
 // every thread of the CTA must call it.  Returns false (error recorded) when a flag never
 // arrived.
@@ -164,7 +180,7 @@ __global__ void __launch_bounds__(256) exchange_counts_kernel(P2PArgs a, const i
     const int r = i / a.E, e = i - r * a.E;
     reinterpret_cast<int32_t*>(peer_base(a, r) + a.off_cnt)[a.me * a.E + e] = counts[e];
   }
-  __threadfence_system();
+  if (tid < a.ep * a.E) __threadfence_system();   // only the threads that stored to peers
   __syncthreads();
   if (tid == 0)
     for (int r = 0; r < a.ep; ++r) st_release_sys(flag_ptr(a, r, kFlagCounts, a.me), epoch);
@@ -242,7 +258,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(P2PArgs a, const uint4* _
       src = x + t * vec;
       dst = reinterpret_cast<uint4*>(peer_base(a, a.me) + a.off_rows) + (a.routed_rows + s * a.T + t) * vec;
     }
-    for (int c = lane; c < vec; c += 32) dst[c] = __ldg(src + c);
+    copy_row(dst, src, vec, lane);
   }
   signal_when_grid_done(a, kFlagRows, a.state + 2, epoch);
 }
@@ -262,7 +278,7 @@ __global__ void __launch_bounds__(256) send_back_kernel(P2PArgs a, const uint4* 
     if (s >= a.ep || slot >= a.Tc * a.k) { if (lane == 0) report_error(reinterpret_cast<uint32_t*>(a.state + 1), kErrBadArg, kSite + 5); continue; }
     uint4* dst = reinterpret_cast<uint4*>(peer_base(a, s) + a.off_ret) + (int64_t)slot * vec;
     const uint4* src = out + q * vec;
-    for (int c = lane; c < vec; c += 32) dst[c] = src[c];
+    copy_row(dst, src, vec, lane);
   }
   signal_when_grid_done(a, kFlagReturns, a.state + 3, epoch);
 }
