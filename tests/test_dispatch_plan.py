@@ -99,3 +99,23 @@ def test_plan_kernels_match_torch(ep, epr, T, k, C, S, full):
     assert torch.equal(send, send_t) and torch.equal(comb, comb_t)
     for a, b in zip(plan, plan_t):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("ep,Tc,E,k,expect", [
+    (1, 64, 8, 2, (64, 64)),        # 16 rows per expert: decode kernels for both GEMMs
+    (2, 64, 8, 2, (64, 64)),        # 32 rows
+    (4, 64, 8, 2, (65, 64)),        # 64 rows: prefill tiles for gate/up, decode down
+    (8, 64, 8, 2, (128, 64)),       # 128 rows: still the decode down GEMM
+    (8, 96, 8, 2, (192, 192)),      # 192 rows: prefill tiles for both (down fused with the return)
+    (2, 8192, 8, 2, (4096, 4096)),  # prefill step
+    (4, 9, 64, 6, (64, 64)),        # fine-grained decode: 3 rows per expert
+])
+def test_gemm_kernel_choice_follows_expected_rows_per_expert(ep, Tc, E, k, expect):
+    from types import SimpleNamespace
+    from light_moe_b200.expert_parallel import DECODE_MAX_ROWS, ExpertParallelW4A16Layer
+    layer = SimpleNamespace(config=SimpleNamespace(top_k=k, num_experts=E), ep_group=SimpleNamespace(ep_size=ep),
+                            capacity_tokens=Tc)
+    gu, dn = ExpertParallelW4A16Layer._gemm_hints(layer)
+    assert (gu, dn) == expect
+    # a hint <= DECODE_MAX_ROWS selects the decode kernels in the grouped GEMM entry point
+    assert (gu <= DECODE_MAX_ROWS) == (ep * Tc * k // E < DECODE_MAX_ROWS)
