@@ -53,8 +53,10 @@ class PeerExchange:
             capi.call("lmoe_p2p_alloc", nbytes, ctypes.byref(ptr), handle)
         self._own = ptr.value
         self._mapped = []
-        # every rank's IPC handle, gathered over the group (a one-time exchange)
-        h = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        # every rank's IPC handle, gathered over the group (a one-time exchange; NCCL groups
+        # gather device tensors, others host tensors)
+        on_dev = dist.get_backend(self.pg) == "nccl"
+        h = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device if on_dev else "cpu")
         gathered = [torch.empty_like(h) for _ in range(self.ep)]
         dist.all_gather(gathered, h, group=self.pg)
         bases = []
@@ -97,6 +99,9 @@ class PeerExchange:
                   self.seg_offsets.data_ptr(), self.dst_base.data_ptr(), capi.stream_handle())
 
     def dispatch(self, x: torch.Tensor, sorted_idx, ids, offsets):
+        if x.dtype != torch.bfloat16 or x.device != self.device or not x.is_contiguous():
+            raise ValueError("the peer-memory exchange moves contiguous bf16 rows on its device "
+                             "(the W4A16 GEMMs' input type)")
         T = x.shape[0]
         capi.call("lmoe_p2p_dispatch", *self._args(T), x.data_ptr() if T else None,
                   sorted_idx.data_ptr() if T else None, ids.data_ptr() if T else None,
