@@ -113,6 +113,8 @@ class HostBufferCalls:
         neighbouring calls' kernels already hide the copies, and whole-batch GEMM tiles are
         fuller (8192 tokens of the Mixtral layer: 5.42-5.50 ms per call against 5.78-5.86
         with 2-3 ranges, 5.24 ms device-only)."""
+        if not self._host_ranges and chunks != 1:
+            raise ValueError("this layer runs every call as one token range (chunks=1)")
         if x_host.device.type != "cpu":
             raise ValueError("forward_host takes host activations; use forward for device tensors")
         if x_host.dtype != torch.bfloat16:
@@ -135,8 +137,6 @@ class HostBufferCalls:
             self._copy_streams = (torch.cuda.Stream(device), torch.cuda.Stream(device))
         h2d, d2h = self._copy_streams
         done = torch.cuda.Event()
-        if not self._host_ranges and chunks != 1:
-            raise ValueError("this layer runs every call as one token range (chunks=1)")
         n = 1 if T <= SMALL_BATCH_TOKENS else max(1, min(int(chunks), T // (SMALL_BATCH_TOKENS + 1)))
         bounds = [T * i // n for i in range(n + 1)]
         loaded = []

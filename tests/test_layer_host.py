@@ -43,3 +43,14 @@ def test_small_batch_threshold_matches_the_router():
     from pathlib import Path
     src = (Path(__file__).resolve().parents[1] / "light_moe_b200" / "csrc" / "router.cu").read_text()
     assert int(re.search(r"constexpr int kSmallTokens = (\d+);", src).group(1)) == SMALL_BATCH_TOKENS
+
+
+def test_expert_parallel_host_calls_are_one_range():
+    # every rank must take the same steps, so the expert-parallel layer refuses to split a
+    # host call into token ranges (checked before any device work)
+    from light_moe_b200.expert_parallel import ExpertParallelW4A16Layer
+    layer = ExpertParallelW4A16Layer.__new__(ExpertParallelW4A16Layer)
+    with pytest.raises(ValueError, match="one token range"):
+        layer.forward_host_async(torch.zeros(4, 64, dtype=torch.bfloat16), chunks=2)
+    with pytest.raises(ValueError, match="one token range"):
+        layer.forward_host(torch.zeros(4, 64, dtype=torch.bfloat16), chunks=3)
